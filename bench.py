@@ -1,0 +1,421 @@
+"""Forward-throughput benchmark of the enGPT hot path on B200.
+
+Workload (one "step"): ``EfficientNGPT`` forward + token cross-entropy under
+bf16 autocast, L=16, d=1024, H=16 (head_dim 64), T=2048, vocab 50257, batch
+32 sequences per GPU, random-init unit-sphere weights (seed 0) and uniform
+random token ids (synthetic data).  Multi-GPU runs are weak-scaled: each rank
+runs its own 32-sequence shard (batch split, no collective inside the hot
+path); one NCCL all-reduce of the scalar loss per step gathers the result.
+
+Reported (one JSON line from rank 0):
+  value      tokens/s over all ranks, inputs resident in HBM, device-timed
+             with CUDA events (max over ranks)
+  e2e        the same metric through the public API (``model(idx, targets)``)
+             with pinned host ids/targets copied in and the loss copied out
+             inside the timed region
+  roofline   the attention kernel (tcgen05) against bf16 tensor peak
+  kernels    per-kernel averages of the other CUDA kernels (HBM roofline)
+  cpu_baseline  the oracle's fp32 numpy forward on the host cores (N=1 only)
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port) on the host cores for the same workload and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "forward tokens/sec (EfficientNGPT bf16, L=16 d=1024 H=16 T=2048)"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["engpt_b200", "reference"], default="engpt_b200")
+    ap.add_argument("--batch", type=int, default=32, help="sequences per GPU")
+    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--dim", type=int, default=1024)
+    ap.add_argument("--vocab", type=int, default=50257)
+    ap.add_argument("--cpu-sample-seqs", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(a, world):
+    return {
+        "workload": (f"EfficientNGPT forward + cross-entropy, bf16 autocast, L={a.layers} d={a.dim} H={a.heads} "
+                     f"T={a.seq} V={a.vocab}, {a.batch} sequences per GPU"),
+        "global_batch": a.batch * world,
+        "seq_len": a.seq,
+        "parallelism": f"dp{world} (batch shard per GPU, no collective in the hot path)",
+        "l2": "no flush: activations per step (~10 GB) exceed the 126 MB L2",
+    }
+
+
+def model_config(a):
+    from engpt_b200 import ModelConfig
+    return ModelConfig(vocab_size=a.vocab, block_size=a.seq, n_layer=a.layers, n_head=a.heads, n_embd=a.dim,
+                       mlp_ratio=4.0, dropout=0.0)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "attention_tcgen05_L16_d1024_T2048.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# -------------------------------------------------------------- CPU baseline
+def cpu_baseline(a, n_seqs):
+    """The oracle (numpy fp32 restatement of the reference forward) on the host cores."""
+    import torch
+    from oracle import ngpt_oracle as O
+    from engpt_b200 import EfficientNGPT
+
+    torch.manual_seed(0)
+    model = EfficientNGPT(model_config(a))
+    w = {k: v.detach().numpy() for k, v in model.state_dict().items()}
+    del model
+    cfg = O.OracleConfig(vocab_size=a.vocab, block_size=a.seq, n_layer=a.layers, n_head=a.heads, n_embd=a.dim)
+    gen = torch.Generator().manual_seed(0)
+    idx = torch.randint(0, a.vocab, (n_seqs, a.seq), generator=gen).numpy()
+    tgt = np.roll(idx, -1, axis=1)
+    t0 = time.perf_counter()
+    _, loss, _ = O.efficient_ngpt_forward(cfg, w, idx, tgt, dtype=np.float32)
+    dt = time.perf_counter() - t0
+    return n_seqs * a.seq / dt, dt, loss
+
+
+def run_reference(a, world, rank):
+    if rank != 0:
+        return
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    from oracle import ngpt_oracle as O
+    from engpt_b200 import EfficientNGPT
+
+    torch.manual_seed(0)
+    model = EfficientNGPT(model_config(a))
+    w = {k: v.detach().numpy() for k, v in model.state_dict().items()}
+    del model
+    cfg = O.OracleConfig(vocab_size=a.vocab, block_size=a.seq, n_layer=a.layers, n_head=a.heads, n_embd=a.dim)
+    gen = torch.Generator().manual_seed(0)
+    n = a.cpu_sample_seqs
+    idx = torch.randint(0, a.vocab, (n, a.seq), generator=gen).numpy()
+    tgt = np.roll(idx, -1, axis=1)
+    for _ in range(a.warmup):
+        O.efficient_ngpt_forward(cfg, w, idx, tgt, dtype=np.float32)
+    times = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        O.efficient_ngpt_forward(cfg, w, idx, tgt, dtype=np.float32)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = a.steps * n * a.seq / total
+    sample = f"{n} x {a.seq}-token sequence(s) of the workload per step, fp32 numpy, {cores} threads"
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": 1000.0 * total / a.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(a, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+# kernels launched per C-ABI call
+LAUNCHES = {"engpt_cross_entropy": 2}
+
+
+def run_gpu(a, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+    from engpt_b200 import EfficientNGPT, _lib
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    cfg = model_config(a)
+    torch.manual_seed(0)
+    model = EfficientNGPT(cfg).to(dev).eval().requires_grad_(False)
+    gen = torch.Generator().manual_seed(1000 + rank)
+    idx_h = torch.randint(0, cfg.vocab_size, (a.batch, a.seq), generator=gen)
+    tgt_h = torch.roll(idx_h, -1, dims=1)
+    idx_d, tgt_d = idx_h.to(dev), tgt_h.to(dev)
+
+    # count our kernel launches through the C-ABI
+    counter = {"n": 0}
+    real_call = _lib.call
+
+    def counting_call(name, *args):
+        counter["n"] += LAUNCHES.get(name, 1)
+        return real_call(name, *args)
+
+    _lib.call = counting_call
+
+    def step(idx, tgt):
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, loss = model(idx, tgt)
+        if world > 1:
+            dist.all_reduce(loss, op=dist.ReduceOp.SUM)
+            loss = loss / world
+        return logits, loss
+
+    for _ in range(max(a.warmup, 1)):
+        step(idx_d, tgt_d)
+    torch.cuda.synchronize()
+
+    # attention launch timing inside the timed region
+    attn_events = []
+
+    def attn_timer(kind):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        attn_events.append(ev)
+
+    model.attn_timer = attn_timer
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    counter["n"] = 0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        logits, loss = step(idx_d, tgt_d)
+        del logits
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = counter["n"]
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    model.attn_timer = None
+    ms = ev0.elapsed_time(ev1)
+    attn_ms = [attn_events[i].elapsed_time(attn_events[i + 1]) for i in range(0, len(attn_events), 2)]
+    attn_avg = sum(attn_ms) / max(len(attn_ms), 1)
+    loss_val = float(loss.item())
+
+    # end-to-end through the public API: pinned host inputs in, loss out, every step
+    idx_p, tgt_p = idx_h.pin_memory(), tgt_h.pin_memory()
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    step(idx_p, tgt_p)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        _, loss = step(idx_p, tgt_p)
+        loss_h.copy_(loss, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # per-kernel averages of the HBM-bound kernels (one instrumented forward, outside the timed region)
+    kern = profile_kernels(model, step, idx_d, tgt_d, cfg, a)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, attn_avg], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, attn_avg = t.tolist()
+
+    if rank != 0:
+        return
+    tokens = a.batch * a.seq * world * a.steps
+    value = tokens / (ms / 1000.0)
+    e2e = tokens / (e2e_ms / 1000.0)
+    peaks = load_peaks()
+    Dh = a.dim // a.heads
+    attn_flops = 2.0 * a.batch * a.heads * a.seq * a.seq * Dh  # causal: QK^T and PV over the lower triangle
+    achieved = attn_flops / (attn_avg / 1000.0) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (uniform random ids, seeded random-init unit-sphere weights)",
+        "config": workload_config(a, world),
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * idx_h.numel() * idx_h.element_size() * world,
+                "d2h_bytes_per_step": 4 * world},
+        "gpu_launches": launches,
+        "roofline": {"kernel": "attn_fwd_kernel<64> (tcgen05)", "bound": "tensor", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(),
+                     "peak_source": f"{peaks['source']} bf16 sustained",
+                     "avg_launch_ms": attn_avg, "flops_per_launch": attn_flops},
+        "kernels": kern,
+        "loss": loss_val,
+        "clocks": clocks,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        try:
+            tps, dt, _ = cpu_baseline(a, a.cpu_sample_seqs)
+            out["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                   "sample": f"{a.cpu_sample_seqs} x {a.seq}-token sequence(s), fp32 numpy oracle, "
+                                             f"{dt:.1f} s"}
+        except Exception as exc:  # pragma: no cover - reported, not fatal
+            out["cpu_baseline"] = {"error": repr(exc)}
+    print(json.dumps(out), flush=True)
+
+
+def profile_kernels(model, step, idx, tgt, cfg, a):
+    """Average device time per launch of each C-ABI entry point over one forward (events around each call)."""
+    import torch
+    from engpt_b200 import _lib
+
+    per = {}
+    real = _lib.call
+
+    def timed(name, *args):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = real(name, *args)
+        e1.record()
+        per.setdefault(name, []).append((e0, e1))
+        return r
+
+    _lib.call = timed
+    try:
+        step(idx, tgt)
+        torch.cuda.synchronize()
+    finally:
+        _lib.call = real
+    n = a.batch * a.seq
+    d = a.dim
+    peaks = load_peaks()
+    # algorithmic bytes per launch (dtypes as used by the engine)
+    alg = {
+        "engpt_carried_residual_gauge": (4 + 2 + 4 + 2) * n * d + 8 * n,   # Y in/out fp32, branch + aux bf16
+        "engpt_qkv_postprocess": 12 * n * d + 4 * n,                      # qkv bf16 in, q/k/v bf16 out, rho
+        "engpt_swiglu": (4 + 2) * n * 4 * d,                              # ug bf16 in (2W), out bf16 (W)
+        "engpt_cross_entropy": 2 * n * a.vocab + 12 * n,
+        "engpt_embed_carried": (4 + 4 + 2) * n * d + 12 * n,
+    }
+    out = {}
+    for name, evs in per.items():
+        ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+        avg = sum(ms) / len(ms)
+        rec = {"launches_per_step": len(ms), "avg_ms": avg}
+        if name in alg:
+            gbs = alg[name] / (avg / 1000.0) / 1e9
+            rec.update({"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"],
+                        "bytes_per_launch": alg[name]})
+        out[name.replace("engpt_", "")] = rec
+    return out
+
+
+def main():
+    a = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.gpus != world and world > 1:
+        print(f"warning: --gpus {a.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    if a.impl == "reference":
+        run_reference(a, world, rank)
+        return
+    import datetime
+    import torch.distributed as dist
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        run_gpu(a, world, rank, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

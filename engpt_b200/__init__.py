@@ -1,0 +1,20 @@
+"""B200-native (sm_100a) forward hot path of enGPT (carried-radius nGPT).
+
+Drop-in names for the reference package:
+
+* ``ModelConfig`` -- engpt/config.py
+* ``EfficientNGPT`` / ``EfficientNGPTBlock`` -- engpt/models.py (same
+  ``state_dict`` keys and seeded init; forward runs the fused CUDA engine)
+* ``engpt_b200.kernels`` -- the engpt.kernels hot-path ops on CUDA kernels
+* ``patch_reference(engpt_pkg)`` -- rebinds the hot-path ops inside an
+  imported reference package so its own model calls the CUDA kernels
+"""
+
+__version__ = "0.1.0"
+
+from .config import ModelConfig
+from .models import EfficientNGPT, EfficientNGPTBlock
+from . import kernels
+from .integration import patch_reference
+
+__all__ = ["EfficientNGPT", "EfficientNGPTBlock", "ModelConfig", "kernels", "patch_reference", "__version__"]

@@ -1,0 +1,421 @@
+// Causal flash attention for B200 (sm_100a): tcgen05 MMA with TMEM
+// accumulators, TMA-staged Q/K/V tiles, online softmax in registers.
+//
+// Computes causal_sdpa (engpt/kernels.py:417-431) with the nGPT scale
+// sqrt(Dh) (engpt/kernels.py:434-435) for bf16 inputs and head_dim 64 / 128.
+//
+// One CTA owns a 128-query tile of one (batch, head) and walks the causal
+// prefix of 128-key tiles.  Warp roles (192 threads):
+//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1      TMEM allocator + MMA issuer (one thread):
+//                 S_j = Q K_j^T       -> TMEM S[j % 2]   (fp32, 128 columns)
+//                 O  += P_{j-1} V_{j-1} -> TMEM O        (fp32, Dh columns)
+//   warps 2..5  softmax: thread i owns query row i (TMEM lane i); reads S_j
+//               with tcgen05.ld, applies the causal mask, exponentiates in
+//               base 2 against a per-row reference max and writes P_j (bf16)
+//               into a 128B-swizzled shared tile, the A operand of the PV MMA.
+// The per-row reference max is only raised (rescaling O in TMEM) when the
+// tile max exceeds it by more than 2^8, so the usual case does no O round
+// trip; exponentials stay <= 256 and the final O / l is exact.
+// Every wait is bounded (see mbar_wait); on a timeout the kernel records
+// ENGPT_ERR_TIMEOUT in the device status word, drains its own copies and
+// MMAs, frees TMEM and returns.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace engpt {
+
+int launch_attn_simt(const void* q, const void* k, const void* v, void* o, int dtype, int B, int T, int H, int Dh,
+                     float scale, const int64_t* strides, cudaStream_t st);
+
+namespace attn_tc {
+
+using namespace sm100;
+
+constexpr int BM = 128;              // queries per CTA tile
+constexpr int BN = 128;              // keys per KV tile
+constexpr int NS = 2;                // K/V pipeline stages
+constexpr int kThreads = 192;
+constexpr int kBlockBytes = 128 * 128;  // one 128-row x 64-col bf16 SW128 block
+
+template <int D>
+struct Layout {
+  static constexpr int kDB = D / 64;                       // 64-col blocks per row
+  static constexpr int Q = 0;
+  static constexpr int K = Q + kDB * kBlockBytes;          // NS stages
+  static constexpr int V = K + NS * kDB * kBlockBytes;     // NS stages
+  static constexpr int P = V + NS * kDB * kBlockBytes;     // 2 buffers x 2 blocks (128 keys)
+  static constexpr int BAR = P + 2 * 2 * kBlockBytes;
+  static constexpr int kBars = 16;
+  static constexpr int MISC = BAR + kBars * 8;             // tmem slot, abort word
+  static constexpr int TOTAL = MISC + 16;
+  static constexpr int kDynSmem = TOTAL + 1024;            // + alignment slack
+};
+
+// barrier indices
+enum {
+  B_Q = 0,
+  B_KFULL = 1,   // + stage
+  B_VFULL = 3,   // + stage
+  B_KVEMPTY = 5, // + stage
+  B_SFULL = 7,   // + buffer
+  B_PFULL = 9,   // + buffer
+  B_PVDONE = 11, // + buffer
+  B_FINAL = 13
+};
+
+struct Params {
+  __nv_bfloat16* o;
+  int64_t os_b, os_t, os_h;
+  int B, T, H;
+  int n_qt;
+  float scale_log2;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using L = Layout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::BAR + 8 * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // heaviest (longest causal prefix) tiles first
+  const int bh_count = p.B * p.H;
+  const int lin = blockIdx.x;
+  const int qt = p.n_qt - 1 - lin / bh_count;
+  const int bh = lin % bh_count;
+  const int b = bh / p.H;
+  const int h = bh % p.H;
+  const int q0 = qt * BM;
+  const int n_kv = qt + 1;  // BM == BN: causal prefix of tile qt
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B_Q), 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(B_KFULL + s), 1);
+      mbar_init(bar(B_VFULL + s), 1);
+      mbar_init(bar(B_KVEMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_SFULL + i), 1);
+      mbar_init(bar(B_PFULL + i), 128);
+      mbar_init(bar(B_PVDONE + i), 1);
+    }
+    mbar_init(bar(B_FINAL), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;          // S buffers: columns [0,128) and [128,256)
+  const uint32_t tO = tmem + 256;    // O: columns [256, 256 + D)
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(bar(B_Q), BM * D * 2);
+      for (int db = 0; db < L::kDB; ++db)
+        tma_load_4d(sbase + L::Q + db * kBlockBytes, &tmQ, db * 64, q0, h, b, bar(B_Q));
+      int last_use[NS];
+      for (int s = 0; s < NS; ++s) last_use[s] = -1;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % NS;
+        if (j >= NS) {
+          ok = mbar_wait(bar(B_KVEMPTY + s), ((j / NS) - 1) & 1, abort_flag, 1);
+          if (!ok) break;
+        }
+        mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
+        for (int db = 0; db < L::kDB; ++db)
+          tma_load_4d(sbase + L::K + (s * L::kDB + db) * kBlockBytes, &tmK, db * 64, j * BN, h, b,
+                      bar(B_KFULL + s));
+        mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
+        for (int db = 0; db < L::kDB; ++db)
+          tma_load_4d(sbase + L::V + (s * L::kDB + db) * kBlockBytes, &tmV, db * 64, j * BN, h, b,
+                      bar(B_VFULL + s));
+        last_use[s] = j / NS;
+      }
+      if (!ok || *abort_flag) {
+        // drain every copy this thread issued before shared memory goes away
+        volatile int never = 0;
+        mbar_wait(bar(B_Q), 0, &never, 0);
+        for (int s = 0; s < NS; ++s) {
+          if (last_use[s] >= 0) {
+            mbar_wait(bar(B_KFULL + s), last_use[s] & 1, &never, 0);
+            mbar_wait(bar(B_VFULL + s), last_use[s] & 1, &never, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescS = idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t kIdescPV = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, 2);
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          const int s = j % NS;
+          const int sb = j & 1;
+          ok = mbar_wait(bar(B_KFULL + s), (j / NS) & 1, abort_flag, 3);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qa = sbase + L::Q + (kk >> 2) * kBlockBytes + (kk & 3) * 32;
+            const uint32_t ka = sbase + L::K + (s * L::kDB + (kk >> 2)) * kBlockBytes + (kk & 3) * 32;
+            umma_f16_ss(tS + sb * BN, sw128_desc(qa, 16, 1024), sw128_desc(ka, 16, 1024), kIdescS, kk > 0);
+          }
+          umma_commit(bar(B_SFULL + sb));
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int s2 = jj % NS;
+          const int pb = jj & 1;
+          ok = mbar_wait(bar(B_PFULL + pb), (jj >> 1) & 1, abort_flag, 4);
+          if (!ok) break;
+          ok = mbar_wait(bar(B_VFULL + s2), (jj / NS) & 1, abort_flag, 5);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint32_t pa = sbase + L::P + (pb * 2 + (kk >> 2)) * kBlockBytes + (kk & 3) * 32;
+            const uint32_t va = sbase + L::V + s2 * L::kDB * kBlockBytes + kk * 16 * 128;
+            umma_f16_ss(tO, sw128_desc(pa, 16, 1024), sw128_desc(va, kBlockBytes, 1024), kIdescPV,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bar(B_PVDONE + pb));
+          umma_commit(bar(B_KVEMPTY + s2));
+        }
+      }
+      // all MMAs of this thread complete before TMEM is released
+      umma_commit(bar(B_FINAL));
+      volatile int never = 0;
+      mbar_wait(bar(B_FINAL), 0, &never, 6);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int wq = warp & 3;                 // TMEM lane quarter of this warp
+    const int row = wq * 32 + lane;          // query row within the tile
+    const int q_idx = q0 + row;
+    const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      ok = mbar_wait(bar(B_SFULL + sb), (j >> 1) & 1, abort_flag, 7);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t r[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) tmem_ld32(tS + t_lane + sb * BN + c, r + c);
+      tmem_wait_ld();
+      const int kbase = j * BN;
+      if (kbase + BN - 1 > q_idx) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (kbase + c > q_idx) r[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = __uint_as_float(r[0]);
+#pragma unroll
+      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+      const float m_new = mx * sl2;
+      if (j == 0) {
+        m_used = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
+        // raise the reference max: rescale O (complete through PV_{j-1}) and l
+        const float mu = fmaxf(m_used, m_new);
+        const float f = ex2_approx(m_used - mu);
+        ok = mbar_wait(bar(B_PVDONE + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, 8);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tO + t_lane + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st32(tO + t_lane + c, o);
+        }
+        tmem_wait_st();
+        l *= f;
+        m_used = mu;
+      }
+      if (j >= 2) {
+        // P buffer sb was read by PV_{j-2}
+        ok = mbar_wait(bar(B_PVDONE + sb), ((j - 2) >> 1) & 1, abort_flag, 9);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      }
+      uint8_t* pbuf = smem + L::P + sb * 2 * kBlockBytes + row * 128;
+      float sum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < BN / 8; ++c8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = ex2_approx(fmaf(__uint_as_float(r[c8 * 8 + i]), sl2, -m_used));
+          sum += e[i];
+        }
+        uint4 packed;
+        packed.x = pack_bf16x2(e[0], e[1]);
+        packed.y = pack_bf16x2(e[2], e[3]);
+        packed.z = pack_bf16x2(e[4], e[5]);
+        packed.w = pack_bf16x2(e[6], e[7]);
+        const int blk = c8 >> 3;
+        const int ch = c8 & 7;
+        *reinterpret_cast<uint4*>(pbuf + blk * kBlockBytes + ((ch ^ (row & 7)) << 4)) = packed;
+      }
+      l += sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(B_PFULL + sb));
+    }
+    if (ok) {
+      ok = mbar_wait(bar(B_PVDONE + ((n_kv - 1) & 1)), ((n_kv - 1) >> 1) & 1, abort_flag, 10);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      __nv_bfloat16* orow = p.o + (int64_t)b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)h * p.os_h;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(tO + t_lane + c, o);
+        tmem_wait_ld();
+        if (q_idx < p.T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c + i) = v;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// --------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encode() {
+  if (g_encode) return ENGPT_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return set_error(ENGPT_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return ENGPT_OK;
+}
+
+// [D, T, H, B] view of a bf16 tensor with element strides (t, h, b); box 64 x 128.
+static int make_map(CUtensorMap* m, const void* base, int D, int T, int H, int B, int64_t st, int64_t sh,
+                    int64_t sb) {
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ENGPT_ERR_ALIGN, "tensor map encode failed (%d)", (int)r);
+  return ENGPT_OK;
+}
+
+static bool tc_eligible(const void* q, const void* k, const void* v, void* o, int Dh, const int64_t* s) {
+  if (Dh != 64 && Dh != 128) return false;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16)) return false;
+  for (int i = 0; i < 12; ++i)
+    if ((s[i] * 2) % 16 != 0 || s[i] <= 0) return false;
+  return true;
+}
+
+template <int D>
+static int launch(const void* q, const void* k, const void* v, void* o, int B, int T, int H, float scale,
+                  const int64_t* s, cudaStream_t st) {
+  using Lt = Layout<D>;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, q, D, T, H, B, s[1], s[2], s[0]))) return rc;
+  if ((rc = make_map(&mk, k, D, T, H, B, s[4], s[5], s[3]))) return rc;
+  if ((rc = make_map(&mv, v, D, T, H, B, s[7], s[8], s[6]))) return rc;
+  Params p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.os_b = s[9];
+  p.os_t = s[10];
+  p.os_h = s[11];
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.n_qt = (T + BM - 1) / BM;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t blocks = (int64_t)p.n_qt * B * H;
+  ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
+  auto kern = attn_fwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::kDynSmem);
+  if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "attention: smem attribute: %s", cudaGetErrorString(e));
+  kern<<<(unsigned)blocks, kThreads, Lt::kDynSmem, st>>>(mq, mk, mv, p);
+  return check_launch("attention (tcgen05)");
+}
+
+}  // namespace attn_tc
+}  // namespace engpt
+
+using namespace engpt;
+
+extern "C" int engpt_causal_attention(const void* q, const void* k, const void* v, void* o, int dtype, int B, int T,
+                                      int H, int Dh, float scale, const int64_t* strides, int impl, void* stream) {
+  clear_error();
+  ENGPT_REQUIRE(B >= 0 && T >= 0 && H > 0 && Dh > 0, ENGPT_ERR_SHAPE, "attention: B=%d T=%d H=%d Dh=%d", B, T, H, Dh);
+  ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "attention: dtype %d", dtype);
+  ENGPT_REQUIRE(impl >= ENGPT_ATTN_AUTO && impl <= ENGPT_ATTN_SIMT, ENGPT_ERR_ARG, "attention: impl %d", impl);
+  if ((int64_t)B * T == 0) return ENGPT_OK;
+  ENGPT_REQUIRE(q && k && v && o && strides, ENGPT_ERR_ARG, "attention: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const bool tc_ok = dtype == ENGPT_BF16 && attn_tc::tc_eligible(q, k, v, o, Dh, strides);
+  if (impl == ENGPT_ATTN_TCGEN05 && !tc_ok)
+    return set_error(ENGPT_ERR_UNSUPPORTED,
+                     "attention: tcgen05 kernel needs bf16, head_dim 64/128 and 16-byte aligned rows (Dh=%d)", Dh);
+  if (tc_ok && impl != ENGPT_ATTN_SIMT) {
+    int rc = attn_tc::get_encode();
+    if (rc) return rc;
+    if (Dh == 64) return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, st);
+    return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, st);
+  }
+  return launch_attn_simt(q, k, v, o, dtype, B, T, H, Dh, scale, strides, st);
+}

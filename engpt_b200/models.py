@@ -1,0 +1,395 @@
+"""``EfficientNGPT`` with the B200 forward engine.
+
+The module tree, parameter names, shapes, registration order and
+initialisation follow engpt/models.py:111-391, so ``state_dict`` keys match
+the reference and ``torch.manual_seed(s); EfficientNGPT(cfg)`` produces the
+reference's weights bit-for-bit (the init runs on the CPU with the same
+random draws).  ``forward`` / ``forward_carried`` run the carried-radius
+forward (engpt/models.py:263-292) on the GPU:
+
+  per block (engpt/models.py:140-182)
+    qkv      = Y_bf16 @ W_qkv^T                          cuBLAS (plain GEMM)
+    q, k, v  = fused QKV epilogue -> [B,H,T,Dh]          engpt_qkv_postprocess
+    attn     = causal attention  -> [B,T,H,Dh]           engpt_causal_attention (tcgen05)
+    branch   = attn @ W_o^T                              cuBLAS
+    Y, rho   = carried residual + gauge, emits bf16 Y/rho engpt_carried_residual_gauge
+    ug       = (Y/rho)_bf16 @ W_ug^T                     cuBLAS
+    hidden   = SwiGLU epilogue                           engpt_swiglu
+    branch   = hidden @ W_down^T                         cuBLAS
+    Y, rho   = carried residual + gauge, emits bf16 Y    engpt_carried_residual_gauge
+  logits = (Y/rho)_bf16 @ (E_out * s_z_eff)^T_bf16       engpt_scale_rows_cast + cuBLAS
+  loss   = mean token cross-entropy                      engpt_cross_entropy
+
+Precision follows the reference's: under ``torch.autocast("cuda",
+torch.bfloat16)`` the carried state ``Y, rho`` stays fp32, GEMM operands and
+outputs, Q/K/V, attention output and logits are bf16, and the loss is fp32;
+outside autocast everything is fp32.  All activations live in a per-shape
+workspace that is reused across calls; returned logits and loss are fresh.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Callable, Dict, Optional, Tuple
+
+import torch
+from torch import Tensor, nn
+
+from . import _lib
+from . import kernels as K
+from .config import ModelConfig
+
+
+def _ngpt_base_scale(cfg: ModelConfig) -> float:
+    return 1.0 / math.sqrt(float(cfg.n_embd))
+
+
+@torch.no_grad()
+def _normalize_rows_(x: Tensor, eps: float) -> None:
+    # parameter retraction used at init (engpt/kernels.py:98-105, PyTorch path)
+    x.div_(torch.linalg.vector_norm(x, ord=2, dim=-1, keepdim=True).clamp_min(eps))
+
+
+@torch.no_grad()
+def _normalize_columns_(x: Tensor, eps: float) -> None:
+    # engpt/kernels.py:108-116, PyTorch path
+    x.div_(torch.linalg.vector_norm(x, ord=2, dim=0, keepdim=True).clamp_min(eps))
+
+
+class EfficientNGPTBlock(nn.Module):
+    """One carried-radius nGPT block; parameters as engpt/models.py:111-126."""
+
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.qkv = nn.Linear(cfg.n_embd, 3 * cfg.n_embd, bias=False)
+        self.out_proj = nn.Linear(cfg.n_embd, cfg.n_embd, bias=False)
+        self.up_gate = nn.Linear(cfg.n_embd, 2 * cfg.mlp_width, bias=False)
+        self.down_proj = nn.Linear(cfg.mlp_width, cfg.n_embd, bias=False)
+        base_scale = _ngpt_base_scale(cfg)
+        self.alpha_init_value = cfg.alpha_init
+        self.scalar_init_scaling = base_scale
+        self.alpha_attn_raw = nn.Parameter(torch.full((cfg.n_embd,), base_scale))
+        self.alpha_mlp_raw = nn.Parameter(torch.full((cfg.n_embd,), base_scale))
+        self.s_qk = nn.Parameter(torch.full((cfg.n_head, cfg.head_dim), base_scale))
+        self.s_u = nn.Parameter(torch.ones(cfg.mlp_width))
+        self.s_gate = nn.Parameter(torch.ones(cfg.mlp_width))
+
+    # effective scalars (engpt/models.py:128-138), as multipliers on the raw parameters
+    @property
+    def alpha_mult(self) -> float:
+        return self.alpha_init_value / self.scalar_init_scaling
+
+    @property
+    def qk_mult(self) -> float:
+        return 1.0 / self.scalar_init_scaling
+
+    @property
+    def alpha_attn(self) -> Tensor:
+        return self.alpha_attn_raw.abs() * self.alpha_mult
+
+    @property
+    def alpha_mlp(self) -> Tensor:
+        return self.alpha_mlp_raw.abs() * self.alpha_mult
+
+    @property
+    def qk_scale(self) -> Tensor:
+        return self.s_qk * self.qk_mult
+
+    def forward(self, y: Tensor, rho: Tensor, cos: Tensor, sin: Tensor) -> Tuple[Tensor, Tensor]:
+        """engpt/models.py:140-182 through the engpt_b200 ops (standalone block call)."""
+        cfg = self.cfg
+        bsz, seq_len, _ = y.shape
+        qkv = self.qkv(y).view(bsz, seq_len, 3, cfg.n_head, cfg.head_dim)
+        q, k, v = K.qkv_postprocess_from_carried(qkv, rho, cos, sin, self.qk_scale, cfg.norm_eps)
+        attn = K.causal_sdpa(q, k, v, scale=K.ngpt_attention_scale(cfg.head_dim), dropout_p=0.0)
+        branch = self.out_proj(attn.reshape(bsz, seq_len, -1))
+        y, rho = K.carried_residual_gauge(y, rho, branch, self.alpha_attn, cfg.norm_eps, cfg.norm_eps,
+                                          cfg.carried_gauge_max)
+        hidden = K.carried_up_gate_swiglu(y, rho, self.up_gate.weight, self.s_u, self.s_gate,
+                                          sqrt_d=math.sqrt(float(cfg.n_embd)),
+                                          scale_u_by_sqrt_d=cfg.scale_mlp_u_by_sqrt_d)
+        branch = self.down_proj(hidden)
+        return K.carried_residual_gauge(y, rho, branch, self.alpha_mlp, cfg.norm_eps, cfg.norm_eps,
+                                        cfg.carried_gauge_max)
+
+    @torch.no_grad()
+    def project_parameters_(self, eps: float = 1e-12) -> None:
+        """engpt/models.py:223-230."""
+        _normalize_rows_(self.qkv.weight, eps)
+        _normalize_columns_(self.out_proj.weight, eps)
+        _normalize_rows_(self.up_gate.weight, eps)
+        _normalize_columns_(self.down_proj.weight, eps)
+
+
+class _Workspace:
+    """Activation buffers for one (batch, seq_len, precision) shape on one device."""
+
+    def __init__(self, cfg: ModelConfig, bsz: int, seq_len: int, device: torch.device, bf16: bool):
+        d, H, Dh, W = cfg.n_embd, cfg.n_head, cfg.head_dim, cfg.mlp_width
+        n = bsz * seq_len
+        act = torch.bfloat16 if bf16 else torch.float32
+        e = lambda *shape, dtype=act: torch.empty(*shape, device=device, dtype=dtype)  # noqa: E731
+        self.key = (bsz, seq_len, bf16, device)
+        self.bsz, self.seq_len, self.n = bsz, seq_len, n
+        self.act = act
+        self.y = e(n, d, dtype=torch.float32)
+        self.rho = e(n, dtype=torch.float32)
+        self.x = e(n, d)                      # GEMM operand: Y (QKV) or Y/rho (up/gate, head)
+        self.qkv = e(n, 3 * d)
+        self.q = e(bsz, H, seq_len, Dh)
+        self.k = e(bsz, H, seq_len, Dh)
+        self.v = e(bsz, H, seq_len, Dh)
+        self.attn = e(n, d)                   # [B, T, H, Dh]
+        self.branch = e(n, d)
+        self.ug = e(n, 2 * W)
+        self.hidden = e(n, W)
+        self.row_loss = e(n, dtype=torch.float32)
+        self.cos = e(seq_len, Dh // 2, dtype=torch.float32)
+        self.sin = e(seq_len, Dh // 2, dtype=torch.float32)
+        q4, o4 = self.q, self.attn.view(bsz, seq_len, H, Dh)
+        self.attn_strides = torch.tensor(
+            [q4.stride(0), q4.stride(2), q4.stride(1)] * 3 + [o4.stride(0), o4.stride(1), o4.stride(2)],
+            dtype=torch.int64)
+        # bf16 weight copies (re-cast from the fp32 parameters on every forward)
+        if bf16:
+            self.w = [dict(qkv=e(3 * d, d), out=e(d, d), ug=e(2 * W, d), down=e(d, W)) for _ in range(cfg.n_layer)]
+        else:
+            self.w = None
+        self.w_head = e(cfg.vocab_size, d)
+
+
+class EfficientNGPT(nn.Module):
+    """Carried-radius nGPT (engpt/models.py:233-391) with a fused B200 forward."""
+
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.gradient_checkpointing = False
+        self.token_emb = nn.Embedding(cfg.vocab_size, cfg.n_embd)
+        self.blocks = nn.ModuleList([EfficientNGPTBlock(cfg) for _ in range(cfg.n_layer)])
+        self.output_emb = nn.Parameter(torch.empty(cfg.vocab_size, cfg.n_embd))
+        self.scalar_init_scaling = _ngpt_base_scale(cfg)
+        self.logit_scale_init_value = cfg.logit_scale_init
+        self.s_z = nn.Parameter(torch.full((cfg.vocab_size,), self.scalar_init_scaling))
+        self.apply(self._init_weights)
+        nn.init.normal_(self.output_emb, mean=0.0, std=0.02)
+        self.project_parameters_()
+        self._ws: Optional[_Workspace] = None
+        self.attn_impl = _lib.ATTN_AUTO
+        # optional instrumentation: called around the attention launch of every layer
+        self.attn_timer: Optional[Callable[[str], None]] = None
+
+    def _init_weights(self, module: nn.Module) -> None:
+        if isinstance(module, (nn.Linear, nn.Embedding)):
+            nn.init.normal_(module.weight, mean=0.0, std=0.02)
+
+    @property
+    def logit_mult(self) -> float:
+        return self.logit_scale_init_value / self.scalar_init_scaling
+
+    @property
+    def logit_scale(self) -> Tensor:
+        return self.s_z * self.logit_mult
+
+    @torch.no_grad()
+    def project_parameters_(self, eps: float = 1e-12) -> None:
+        """engpt/models.py:356-361."""
+        _normalize_rows_(self.token_emb.weight, eps)
+        _normalize_rows_(self.output_emb, eps)
+        for block in self.blocks:
+            block.project_parameters_(eps)
+
+    def set_gradient_checkpointing(self, enabled: bool = True) -> None:
+        self.gradient_checkpointing = enabled
+
+    # ---------------------------------------------------------------- forward
+    def _check_inference(self) -> None:
+        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            raise NotImplementedError(
+                "engpt_b200 EfficientNGPT is a forward-only (inference) engine: call it under torch.no_grad() "
+                "or after model.requires_grad_(False)")
+
+    def forward(self, idx: Tensor, targets: Optional[Tensor] = None) -> Tuple[Tensor, Optional[Tensor]]:
+        """engpt/models.py:263-268: embed, rho = 1, then the carried forward."""
+        self._check_inference()
+        if idx.size(1) > self.cfg.block_size:
+            raise ValueError("sequence length exceeds block_size")
+        return self._run(idx=idx, targets=targets)
+
+    def forward_carried(self, y: Tensor, rho: Tensor,
+                        targets: Optional[Tensor] = None) -> Tuple[Tensor, Optional[Tensor]]:
+        """engpt/models.py:270-292 from an explicit carried state ``(y, rho)`` (any rho > 0)."""
+        self._check_inference()
+        if y.size(1) > self.cfg.block_size:
+            raise ValueError("sequence length exceeds block_size")
+        if rho.shape != y.shape[:2]:
+            raise ValueError("rho must have shape [batch, sequence]")
+        return self._run(y=y, rho=rho, targets=targets)
+
+    @staticmethod
+    def loss_from_logits(logits: Tensor, targets: Optional[Tensor]) -> Optional[Tensor]:
+        """engpt/models.py:328-339 (token targets) on the CUDA cross-entropy kernel."""
+        if targets is None:
+            return None
+        if targets.ndim != logits.ndim - 1:
+            raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
+        v = logits.shape[-1]
+        flat = logits.reshape(-1, v)
+        if flat.stride(-1) != 1:
+            flat = flat.contiguous()
+        t = targets.reshape(-1).to(device=logits.device, dtype=torch.int64).contiguous()
+        row_loss = torch.empty(flat.shape[0], device=logits.device, dtype=torch.float32)
+        loss = torch.empty((), device=logits.device, dtype=torch.float32)
+        with torch.cuda.device(logits.device):
+            _lib.call("engpt_cross_entropy", flat.data_ptr(), _lib.dtype_code(flat.dtype), flat.shape[0], v,
+                      flat.stride(0), t.data_ptr(), row_loss.data_ptr(), loss.data_ptr(),
+                      _lib.stream_handle(logits.device))
+        return loss
+
+    def _workspace(self, bsz: int, seq_len: int, device: torch.device, bf16: bool) -> _Workspace:
+        key = (bsz, seq_len, bf16, device)
+        if self._ws is None or self._ws.key != key:
+            self._ws = None
+            self._ws = _Workspace(self.cfg, bsz, seq_len, device, bf16)
+        return self._ws
+
+    def release_workspace(self) -> None:
+        self._ws = None
+
+    def _mode_bf16(self, device: torch.device) -> bool:
+        p = self.token_emb.weight
+        if p.dtype != torch.float32:
+            raise NotImplementedError(f"engpt_b200 forward runs fp32 parameters (got {p.dtype})")
+        if torch.is_autocast_enabled("cuda"):
+            dt = torch.get_autocast_dtype("cuda")
+            if dt != torch.bfloat16:
+                raise NotImplementedError(f"engpt_b200 forward supports bf16 autocast only (got {dt})")
+            return True
+        return False
+
+    @torch.no_grad()
+    def _run(self, idx: Optional[Tensor] = None, y: Optional[Tensor] = None, rho: Optional[Tensor] = None,
+             targets: Optional[Tensor] = None,
+             layer_callback: Optional[Callable[[int, Tensor, Tensor], None]] = None
+             ) -> Tuple[Tensor, Optional[Tensor]]:
+        cfg = self.cfg
+        dev = self.token_emb.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("engpt_b200 EfficientNGPT runs on CUDA only (no CPU fallback); call .cuda()")
+        bf16 = self._mode_bf16(dev)
+        src = idx if idx is not None else y
+        bsz, seq_len = src.shape[0], src.shape[1]
+        n = bsz * seq_len
+        d, H, Dh, W = cfg.n_embd, cfg.n_head, cfg.head_dim, cfg.mlp_width
+        ws = self._workspace(bsz, seq_len, dev, bf16)
+        st = _lib.stream_handle(dev)
+        act = _lib.dtype_code(ws.act)
+        with torch.cuda.device(dev):
+            # rotary tables (engpt/models.py:280 -> engpt/kernels.py:355-374)
+            if Dh // 2 > 0:
+                _lib.call("engpt_rotary_tables", seq_len, Dh, float(cfg.rope_theta), ws.cos.data_ptr(),
+                          ws.sin.data_ptr(), st)
+            # carried embedding (engpt/models.py:266-267)
+            if idx is not None:
+                ids = idx.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
+                _lib.call("engpt_embed_carried", ids.data_ptr(), self.token_emb.weight.data_ptr(), n, d,
+                          cfg.vocab_size, ws.y.data_ptr(), ws.rho.data_ptr(),
+                          ws.x.data_ptr() if bf16 else None, st)
+            else:
+                ws.y.copy_(y.reshape(n, d))
+                ws.rho.copy_(rho.reshape(n))
+                if bf16:
+                    _lib.call("engpt_scale_rows_cast", ws.y.data_ptr(), None, 1.0, n, d, ws.x.data_ptr(),
+                              _lib.BF16, st)
+            if bf16:
+                for i, blk in enumerate(self.blocks):
+                    w = ws.w[i]
+                    for name, p in (("qkv", blk.qkv.weight), ("out", blk.out_proj.weight),
+                                    ("ug", blk.up_gate.weight), ("down", blk.down_proj.weight)):
+                        _lib.call("engpt_scale_rows_cast", p.data_ptr(), None, 1.0, p.shape[0], p.shape[1],
+                                  w[name].data_ptr(), _lib.BF16, st)
+            scale = K.ngpt_attention_scale(Dh)
+            sqrt_d = math.sqrt(float(d))
+            u_mult = sqrt_d if cfg.scale_mlp_u_by_sqrt_d else 1.0
+            last = len(self.blocks) - 1
+            for i, blk in enumerate(self.blocks):
+                if bf16:
+                    wq, wo, wug, wd = ws.w[i]["qkv"], ws.w[i]["out"], ws.w[i]["ug"], ws.w[i]["down"]
+                    x_in = ws.x
+                else:
+                    wq, wo, wug, wd = blk.qkv.weight, blk.out_proj.weight, blk.up_gate.weight, blk.down_proj.weight
+                    x_in = ws.y
+                torch.mm(x_in, wq.t(), out=ws.qkv)
+                _lib.call("engpt_qkv_postprocess", ws.qkv.data_ptr(), act, ws.rho.data_ptr(), ws.cos.data_ptr(),
+                          ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(), float(blk.qk_mult), float(cfg.norm_eps),
+                          bsz, seq_len, H, Dh, ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(), 1, st)
+                if self.attn_timer is not None:
+                    self.attn_timer("start")
+                _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
+                          ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
+                          self.attn_impl, st)
+                if self.attn_timer is not None:
+                    self.attn_timer("stop")
+                torch.mm(ws.attn, wo.t(), out=ws.branch)
+                _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(), ws.branch.data_ptr(),
+                          act, blk.alpha_attn_raw.data_ptr(), float(blk.alpha_mult), 1, float(cfg.norm_eps),
+                          float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(),
+                          ws.rho.data_ptr(), ws.x.data_ptr(), _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H, st)
+                torch.mm(ws.x, wug.t(), out=ws.ug)
+                _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, blk.s_u.data_ptr(), blk.s_gate.data_ptr(),
+                          float(u_mult), float(sqrt_d), n, W, ws.hidden.data_ptr(), act, st)
+                torch.mm(ws.hidden, wd.t(), out=ws.branch)
+                if i < last:
+                    aux_mode = _lib.AUX_BF16_Y if bf16 else _lib.AUX_NONE
+                else:
+                    aux_mode = _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H
+                _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(), ws.branch.data_ptr(),
+                          act, blk.alpha_mlp_raw.data_ptr(), float(blk.alpha_mult), 1, float(cfg.norm_eps),
+                          float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(),
+                          ws.rho.data_ptr(), ws.x.data_ptr() if aux_mode != _lib.AUX_NONE else None, aux_mode, st)
+                if layer_callback is not None:
+                    layer_callback(i, ws.y.view(bsz, seq_len, d), ws.rho.view(bsz, seq_len))
+            # output head (engpt/kernels.py:209-229 with logit_scale, engpt/models.py:366-368)
+            _lib.call("engpt_scale_rows_cast", self.output_emb.data_ptr(), self.s_z.data_ptr(),
+                      float(self.logit_mult), cfg.vocab_size, d, ws.w_head.data_ptr(), act, st)
+            logits = torch.empty(bsz, seq_len, cfg.vocab_size, device=dev, dtype=ws.act)
+            x_head = ws.x if len(self.blocks) > 0 else None
+            if x_head is None:
+                raise ValueError("n_layer must be positive")
+            torch.mm(x_head, ws.w_head.t(), out=logits.view(n, cfg.vocab_size))
+            loss = None
+            if targets is not None:
+                if targets.ndim != 2:
+                    raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
+                t = targets.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
+                loss = torch.empty((), device=dev, dtype=torch.float32)
+                _lib.call("engpt_cross_entropy", logits.data_ptr(), act, n, cfg.vocab_size, cfg.vocab_size,
+                          t.data_ptr(), ws.row_loss.data_ptr(), loss.data_ptr(), st)
+        return logits, loss
+
+    def forward_with_states(self, idx: Tensor, targets: Optional[Tensor] = None):
+        """Forward that also returns the per-layer carried state ``[(Y, rho), ...]`` (copies)."""
+        states = []
+        logits, loss = self._run(idx=idx, targets=targets,
+                                 layer_callback=lambda i, y, r: states.append((y.clone(), r.clone())))
+        return logits, loss, states
+
+    def parameter_norm_report(self) -> Dict[str, float]:
+        """engpt/models.py:370-391."""
+        with torch.no_grad():
+            max_err = 0.0
+            d, ff = self.cfg.n_embd, self.cfg.mlp_width
+            norms = [torch.linalg.vector_norm(self.token_emb.weight, dim=-1),
+                     torch.linalg.vector_norm(self.output_emb, dim=-1)]
+            for b in self.blocks:
+                q = b.qkv.weight
+                norms += [torch.linalg.vector_norm(q[:d], dim=-1), torch.linalg.vector_norm(q[d:2 * d], dim=-1),
+                          torch.linalg.vector_norm(q[2 * d:], dim=-1),
+                          torch.linalg.vector_norm(b.out_proj.weight, dim=0),
+                          torch.linalg.vector_norm(b.up_gate.weight[:ff], dim=-1),
+                          torch.linalg.vector_norm(b.up_gate.weight[ff:], dim=-1),
+                          torch.linalg.vector_norm(b.down_proj.weight, dim=0)]
+            for nrm in norms:
+                max_err = max(max_err, (nrm - 1.0).abs().max().item())
+            return {"max_unit_norm_error": max_err}

@@ -1,0 +1,165 @@
+/*
+ * engpt_b200 C ABI: the forward hot path of enGPT (carried-radius nGPT) on
+ * B200 (sm_100a).
+ *
+ * Every entry point takes raw device pointers, element counts/strides and a
+ * CUDA stream handle (cudaStream_t passed as void*), launches its kernels on
+ * that stream and returns an engpt_status.  Nothing here allocates device
+ * memory or synchronises the stream; outputs are written into caller-owned
+ * buffers.  On a non-zero status engpt_last_error() returns a message for
+ * the calling thread.
+ *
+ * Reference interface each entry point replaces is cited as
+ * <file>:<lines> inside the Pi-Willie/enGPT project.
+ */
+#ifndef ENGPT_B200_H
+#define ENGPT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ENGPT_API __attribute__((visibility("default")))
+#else
+#define ENGPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types accepted for activations. */
+enum engpt_dtype {
+  ENGPT_F32 = 0,
+  ENGPT_BF16 = 1
+};
+
+enum engpt_status {
+  ENGPT_OK = 0,
+  ENGPT_ERR_SHAPE = 1,       /* sizes inconsistent or out of the supported range */
+  ENGPT_ERR_DTYPE = 2,       /* dtype code not supported by this entry point     */
+  ENGPT_ERR_ALIGN = 3,       /* pointer or stride misaligned for vector/TMA use  */
+  ENGPT_ERR_LAUNCH = 4,      /* CUDA launch error                                */
+  ENGPT_ERR_TIMEOUT = 5,     /* a device-side wait ran out (see engpt_device_status) */
+  ENGPT_ERR_UNSUPPORTED = 6, /* no kernel for this configuration                  */
+  ENGPT_ERR_ARG = 7          /* null pointer or invalid scalar argument          */
+};
+
+/* Auxiliary output of the carried residual (the next GEMM's operand). */
+enum engpt_aux_mode {
+  ENGPT_AUX_NONE = 0,
+  ENGPT_AUX_BF16_Y = 1,  /* bf16(Y_out): input of the next block's QKV projection      */
+  ENGPT_AUX_BF16_H = 2,  /* bf16(Y_out / rho_out): input of up/gate or output head     */
+  ENGPT_AUX_F32_H = 3    /* fp32 Y_out / rho_out (fp32 mode)                            */
+};
+
+/* Attention kernel selection (engpt_causal_attention `impl`). */
+enum engpt_attn_impl {
+  ENGPT_ATTN_AUTO = 0,   /* tcgen05 kernel when bf16 and head_dim in {64,128}, else SIMT */
+  ENGPT_ATTN_TCGEN05 = 1,
+  ENGPT_ATTN_SIMT = 2
+};
+
+/* Message for the last failing call on this host thread ("" if none). */
+ENGPT_API const char* engpt_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+ENGPT_API int engpt_abi_version(void);
+
+/*
+ * Device-side error word of the current device: 0 when no kernel has
+ * recorded a failure; otherwise the code of the first bounded wait that ran
+ * out (ENGPT_ERR_TIMEOUT) with the site in the upper bits.  Synchronises the
+ * device.  engpt_clear_device_status() resets it.
+ */
+ENGPT_API int engpt_device_status(void);
+ENGPT_API int engpt_clear_device_status(void);
+
+/*
+ * qkv_postprocess_from_carried -- engpt/kernels.py:139-179.
+ *
+ * qkv: [B, T, 3, H, Dh] contiguous, dtype `dtype` (raw projection Y W^T).
+ * rho: [B, T] fp32.  cos_tab/sin_tab: [T, rope_half] fp32 (rope_half = Dh/2
+ * rounded down, as rotary_frequencies builds them).  qk_scale: [H, Dh] fp32;
+ * the scale applied is qk_scale * qk_mult (pass 1.0 for an effective scale).
+ * Outputs q, k, v in `dtype`, laid out [B, T, H, Dh] (out_layout 0, the
+ * reference's) or [B, H, T, Dh] (out_layout 1, head-major for attention).
+ */
+ENGPT_API int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rho,
+                          const float* cos_tab, const float* sin_tab, int rope_half,
+                          const float* qk_scale, float qk_mult, float norm_eps,
+                          int B, int T, int H, int Dh,
+                          void* q_out, void* k_out, void* v_out, int out_layout,
+                          void* stream);
+
+/*
+ * causal_sdpa -- engpt/kernels.py:417-431 (softmax(scale * q k^T + causal) v).
+ *
+ * q, k, v, o: element strides (batch, token, head) given in `strides`
+ * (12 int64: q_b, q_t, q_h, k_b, k_t, k_h, v_b, v_t, v_h, o_b, o_t, o_h); the
+ * head_dim axis is contiguous.  dtype ENGPT_BF16 or ENGPT_F32 for all four.
+ */
+ENGPT_API int engpt_causal_attention(const void* q, const void* k, const void* v, void* o,
+                           int dtype, int B, int T, int H, int Dh, float scale,
+                           const int64_t* strides, int impl, void* stream);
+
+/*
+ * carried_residual_gauge -- engpt/kernels.py:277-324 (with the unfused pair
+ * carried_residual 232-274 + gauge_carried_state 327-338 as the
+ * max_radius <= 0 / > 0 cases).
+ *
+ * y, y_out: [rows, d] fp32 (may alias); rho, rho_out: [rows] fp32 (may
+ * alias); branch: [rows, d] in `branch_dtype`.  alpha: [d] fp32, the applied
+ * alpha is (alpha_abs ? |alpha| : alpha) * alpha_mult.  aux_out receives the
+ * engpt_aux_mode side output ([rows, d], bf16 or fp32) when aux_mode != 0.
+ */
+ENGPT_API int engpt_carried_residual_gauge(const float* y, const float* rho, const void* branch,
+                                 int branch_dtype, const float* alpha, float alpha_mult,
+                                 int alpha_abs, float branch_eps, float residual_eps,
+                                 float max_radius, int64_t rows, int d,
+                                 float* y_out, float* rho_out, void* aux_out, int aux_mode,
+                                 void* stream);
+
+/* rotary_frequencies -- engpt/kernels.py:355-374: fp32 cos/sin [T, Dh/2]. */
+ENGPT_API int engpt_rotary_tables(int T, int Dh, float theta, float* cos_out, float* sin_out, void* stream);
+
+/*
+ * EfficientNGPT.forward embedding step -- engpt/models.py:263-268:
+ * y = token_emb[idx] (fp32 [n, d]), rho = 1; aux_bf16 (optional) = bf16(y).
+ * Out-of-range ids are reported through the device status word.
+ */
+ENGPT_API int engpt_embed_carried(const int64_t* idx, const float* emb, int64_t n_tokens, int d,
+                        int64_t vocab, float* y_out, float* rho_out, void* aux_bf16,
+                        void* stream);
+
+/*
+ * carried_up_gate_swiglu epilogue -- engpt/kernels.py:200-206: given the
+ * up/gate projection ug [rows, 2W] (`dtype`), writes
+ * out = (u * s_u * u_mult) * silu(gate * s_gate * gate_mult) in `out_dtype`.
+ */
+ENGPT_API int engpt_swiglu(const void* ug, int dtype, const float* s_u, const float* s_gate,
+                 float u_mult, float gate_mult, int64_t rows, int width,
+                 void* out, int out_dtype, void* stream);
+
+/*
+ * Row-scaled cast for the output head -- engpt/kernels.py:229 and
+ * engpt/models.py:366-368: out[r, :] = src[r, :] * (scale[r] * mult),
+ * written in out_dtype.  With scale == NULL it is a plain cast.
+ */
+ENGPT_API int engpt_scale_rows_cast(const float* src, const float* scale, float mult, int64_t rows,
+                          int64_t cols, void* out, int out_dtype, void* stream);
+
+/*
+ * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).
+ * logits [rows, vocab] with leading dimension ld (elements), `dtype`;
+ * targets int64 [rows].  row_loss [rows] fp32 is caller-provided scratch;
+ * loss_out receives the fp32 mean.
+ */
+ENGPT_API int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t ld,
+                        const int64_t* targets, float* row_loss, float* loss_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ENGPT_B200_H */
