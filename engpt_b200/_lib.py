@@ -45,7 +45,9 @@ SIGNATURES = {
     "engpt_swiglu": (_i, [_p, _i, _p, _p, _f, _f, _i64, _i, _p, _i, _p]),
     "engpt_scale_rows_cast": (_i, [_p, _p, _f, _i64, _i64, _p, _i, _p]),
     "engpt_cross_entropy": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "engpt_cross_entropy_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
 }
+CE_NOALLOC_MAX_ROWS = 262144
 
 
 class EngptError(RuntimeError):

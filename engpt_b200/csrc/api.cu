@@ -6,6 +6,8 @@
 
 #include <string.h>
 
+#include <mutex>
+
 namespace engpt {
 
 static thread_local char t_err[512] = "";
@@ -419,6 +421,64 @@ int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, int64_t voc
   if (rc) return rc;
   mean_loss_kernel<<<1, 1024, 0, st>>>(row_loss, targets, rows, loss_out);
   return check_launch("cross_entropy_mean");
+}
+
+// ------------------------------------------------ cross-entropy, no allocation
+// Per-row loss scratch for engpt_cross_entropy_noalloc, resident in the
+// library's device memory (one copy per device that loads the library).
+static __device__ __align__(256) float g_ce_noalloc_rows[ENGPT_CE_NOALLOC_MAX_ROWS];
+
+// Device address of g_ce_noalloc_rows per device.  In host code the array's
+// name is only a host-side stand-in, never a device address, so the address is
+// looked up once per device with that device current.
+static float* g_ce_noalloc_addr[64] = {nullptr};
+static std::mutex g_ce_noalloc_mu;
+
+static int ce_noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "cross_entropy_noalloc: cudaGetDevice: %s",
+                                         cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(ENGPT_ERR_UNSUPPORTED, "cross_entropy_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_ce_noalloc_mu);
+  if (g_ce_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ce_noalloc_rows);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(ENGPT_ERR_LAUNCH, "cross_entropy_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_ce_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_ce_noalloc_addr[dev];
+  return ENGPT_OK;
+}
+
+int engpt_cross_entropy_noalloc(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t ld,
+                                const int64_t* targets, float* loss_out, void* stream) {
+  clear_error();
+  ENGPT_REQUIRE(rows > 0 && vocab > 0 && ld >= vocab, ENGPT_ERR_SHAPE,
+                "cross_entropy_noalloc: rows=%lld vocab=%lld ld=%lld", (long long)rows, (long long)vocab,
+                (long long)ld);
+  ENGPT_REQUIRE(rows <= ENGPT_CE_NOALLOC_MAX_ROWS, ENGPT_ERR_SHAPE,
+                "cross_entropy_noalloc: %lld rows exceed the fixed scratch of %d rows; use engpt_cross_entropy "
+                "with a caller-provided row buffer", (long long)rows, ENGPT_CE_NOALLOC_MAX_ROWS);
+  ENGPT_REQUIRE(logits && targets && loss_out, ENGPT_ERR_ARG, "cross_entropy_noalloc: null pointer");
+  ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "cross_entropy_noalloc: dtype %d",
+                dtype);
+  float* row_loss = nullptr;
+  int rc = ce_noalloc_scratch(&row_loss);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == ENGPT_BF16) {
+    cross_entropy_rows_kernel<__nv_bfloat16><<<(unsigned)rows, 256, 0, st>>>((const __nv_bfloat16*)logits, rows, vocab,
+                                                                             ld, targets, row_loss);
+  } else {
+    cross_entropy_rows_kernel<float><<<(unsigned)rows, 256, 0, st>>>((const float*)logits, rows, vocab, ld, targets,
+                                                                     row_loss);
+  }
+  rc = check_launch("cross_entropy_noalloc_rows");
+  if (rc) return rc;
+  mean_loss_kernel<<<1, 1024, 0, st>>>(row_loss, targets, rows, loss_out);
+  return check_launch("cross_entropy_noalloc_mean");
 }
 
 }  // extern "C"

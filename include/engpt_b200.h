@@ -158,6 +158,29 @@ ENGPT_API int engpt_scale_rows_cast(const float* src, const float* scale, float 
 ENGPT_API int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t ld,
                         const int64_t* targets, float* row_loss, float* loss_out, void* stream);
 
+/*
+ * Token cross-entropy that allocates nothing and needs no scratch buffer from
+ * the caller.  This entry point has no counterpart in the reference.
+ *
+ * It is for callers that cannot call cudaMalloc: a host that only owns the
+ * logits, targets and loss buffers it was handed (an FFI or embedded runtime
+ * with no device allocator of its own), or a serving loop that must not call
+ * cudaMalloc because it can synchronise the device.  Same arguments and result
+ * as engpt_cross_entropy, without `row_loss`: the per-row losses go to a
+ * fixed array of ENGPT_CE_NOALLOC_MAX_ROWS floats (1 MiB) that lives in the
+ * library's device memory; every GPU that loads the library holds it until the
+ * process exits.  More rows than that are rejected with ENGPT_ERR_SHAPE.
+ *
+ * The first call on each device looks up the array's device address (with
+ * that device current); make that first call before any stream capture.
+ * All calls share the one array and it keeps the last call's contents; each
+ * call writes every entry it reads, so nothing needs clearing.  Calls that
+ * overlap on the GPU (other streams, other threads) race on the array.
+ */
+#define ENGPT_CE_NOALLOC_MAX_ROWS 262144
+ENGPT_API int engpt_cross_entropy_noalloc(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                                          int64_t ld, const int64_t* targets, float* loss_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
