@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["engpt_b200", "reference"], default="engpt_b200")
+    ap.add_argument("--workload", choices=["forward", "attention"], default="forward",
+                    help="forward: the model step (default); attention: the isolated nGPT attention op")
     ap.add_argument("--batch", type=int, default=32, help="sequences per GPU")
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=16)
@@ -395,6 +397,73 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
     return out
 
 
+def run_attention(a, world, rank, local_rank):
+    """Isolated nGPT attention op: B x H x T x Dh causal, bf16, unit q/k scaled by s ~ U(0.9, 1.1), scale sqrt(Dh).
+
+    Defaults to the BASELINE isolated-attention shape via --batch 8 (B=8, H=16, T=2048, Dh=64).
+    Prints tensor-core roofline numbers for the tcgen05 kernel and, for context, torch's bf16 SDPA.
+    """
+    import torch
+    from engpt_b200 import _lib, kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, H, T = a.batch, a.heads, a.seq
+    Dh = a.dim // a.heads
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(B, T, H, Dh, generator=g)
+    k = torch.randn(B, T, H, Dh, generator=g)
+    v = torch.randn(B, T, H, Dh, generator=g)
+    s = torch.rand(Dh, generator=g) * 0.2 + 0.9
+    q = (q / q.norm(dim=-1, keepdim=True) * s).to(dev, torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True) * s).to(dev, torch.bfloat16)
+    v = v.to(dev, torch.bfloat16)
+    scale = math.sqrt(Dh)
+
+    def ours():
+        with torch.no_grad():
+            return K.causal_sdpa(q, k, v, scale=scale, dropout_p=0.0, impl="tcgen05")
+
+    def torch_sdpa():
+        return torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                                                v.transpose(1, 2), is_causal=True, scale=scale)
+
+    def timeit(fn, steps):
+        for _ in range(max(a.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    ms = timeit(ours, a.steps)
+    clocks = sampler.stop()
+    ms_torch = timeit(torch_sdpa, a.steps)
+    assert _lib.device_status() == 0
+    flops = 2.0 * B * H * T * T * Dh
+    peaks = load_peaks()
+    achieved = flops / (ms / 1000.0) / 1e12
+    print(json.dumps({
+        "metric": "isolated nGPT causal attention TFLOP/s", "value": achieved, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (seeded normal q/k/v, unit q/k scaled by U(0.9,1.1))",
+        "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh)",
+                   "l2": "inputs read once per launch; no flush between launches"},
+        "roofline": {"kernel": f"attn_fwd_kernel<{Dh}> (tcgen05)", "bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": None, "peak_source": f"{peaks['source']} bf16 burst"},
+        "torch_sdpa_bf16": {"ms": ms_torch, "tflops": flops / (ms_torch / 1000.0) / 1e12},
+        "clocks": clocks,
+    }), flush=True)
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -404,6 +473,9 @@ def main():
         print(f"warning: --gpus {a.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
     if a.impl == "reference":
         run_reference(a, world, rank)
+        return
+    if a.workload == "attention":
+        run_attention(a, world, rank, local_rank)
         return
     import datetime
     import torch.distributed as dist

@@ -22,7 +22,7 @@ OK = 0
 STATUS_NAMES = {1: "shape", 2: "dtype", 3: "alignment", 4: "launch", 5: "device timeout", 6: "unsupported",
                 7: "argument"}
 AUX_NONE, AUX_BF16_Y, AUX_BF16_H, AUX_F32_H = 0, 1, 2, 3
-ATTN_AUTO, ATTN_TCGEN05, ATTN_SIMT = 0, 1, 2
+ATTN_AUTO, ATTN_TCGEN05, ATTN_SIMT, ATTN_TCGEN05_1TILE = 0, 1, 2, 3
 
 _lock = threading.Lock()
 _lib: Optional[ctypes.CDLL] = None

@@ -89,11 +89,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // heaviest (longest causal prefix) tiles first
-  const int bh_count = p.B * p.H;
+  // the q tiles of one (batch, head) run back to back, heaviest (longest causal prefix) first,
+  // so the K/V tiles they share are re-read from L2 rather than HBM
   const int lin = blockIdx.x;
-  const int qt = p.n_qt - 1 - lin / bh_count;
-  const int bh = lin % bh_count;
+  const int qt = p.n_qt - 1 - lin % p.n_qt;
+  const int bh = lin / p.n_qt;
   const int b = bh / p.H;
   const int h = bh % p.H;
   const int q0 = qt * BM;
@@ -329,6 +329,391 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ============================================================================
+// Head dim 64: two 128-query tiles per CTA (a 256-query band of one (b, h))
+// share every K/V tile.  Two softmax warpgroups (A: rows 0..127, B: rows
+// 128..255) ping-pong against one MMA-issuing thread; S, P and O all live in
+// TMEM (512 columns: S_A | S_B | P_A | P_B | O_A | O_B), P is written with
+// tcgen05.st as packed bf16 and consumed by the PV MMA straight from TMEM, so
+// the softmax never touches shared memory.  The exponentials are split
+// between the MUFU unit (ex2.approx) and an FMA-pipe polynomial (exp2_poly2)
+// on off-diagonal tiles; scale/subtract, row sums and the polynomial use the
+// packed f32x2 FMA/ADD.
+// ============================================================================
+namespace v2 {
+
+constexpr int D = 64;
+constexpr int BN = 128;              // keys per KV tile
+constexpr int NS = 3;                // K/V pipeline stages
+constexpr int kThreads = 384;        // warps 0: TMA, 1: MMA, 2-3: idle, 4-7: softmax A, 8-11: softmax B
+constexpr int kPolyPer16 = 6;        // of every 16 scores on an off-diagonal tile, this many use the polynomial
+
+struct Layout {
+  static constexpr int QA = 0;
+  static constexpr int QB = QA + kBlockBytes;
+  static constexpr int K = QB + kBlockBytes;             // NS stages x 16 KB
+  static constexpr int V = K + NS * kBlockBytes;         // NS stages x 16 KB
+  static constexpr int BAR = V + NS * kBlockBytes;
+  static constexpr int kBars = 24;
+  static constexpr int MISC = BAR + kBars * 8;
+  static constexpr int TOTAL = MISC + 16;
+  static constexpr int kDynSmem = TOTAL + 1024;
+};
+
+enum {
+  B_Q = 0,
+  B_KFULL = 1,                 // + stage (NS)
+  B_VFULL = B_KFULL + NS,      // + stage
+  B_KVEMPTY = B_VFULL + NS,    // + stage
+  B_SFULL = B_KVEMPTY + NS,    // + warpgroup (2): S_w(j) written
+  B_TDONE = B_SFULL + 2,       // + warpgroup: S_w(j) consumed and P_w(j) written (128 arrivals)
+  B_PVDONE = B_TDONE + 2,      // + warpgroup: PV_w(j) complete
+  B_FINAL = B_PVDONE + 2
+};
+static_assert(B_FINAL < Layout::kBars, "barrier slots");
+
+// TMEM columns
+constexpr uint32_t kColS = 0;     // + 128 * w
+constexpr uint32_t kColP = 256;   // + 64 * w   (bf16 pairs: 128 keys in 64 columns)
+constexpr uint32_t kColO = 384;   // + 64 * w
+
+// One 32-score chunk of a row: x = score * scale*log2(e) - m, exponentiate,
+// pack to 16 bf16 pairs, add the pair sums to l2 and track max(x).
+// MIXED sends kPolyPer16 of every 16 scores to the FMA polynomial (only used
+// on tiles without masked scores); otherwise all go to MUFU.
+template <bool MIXED>
+__device__ __forceinline__ void exp_chunk(const uint32_t* r, uint64_t sc2, uint64_t nm2, uint64_t& l2, float& mx,
+                                          uint32_t* pw) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t x = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
+    float x0, x1;
+    f2_unpack(x, x0, x1);
+    mx = fmaxf(mx, fmaxf(x0, x1));
+    uint64_t e;
+    if (MIXED && ((2 * i) & 15) < kPolyPer16) {
+      e = exp2_poly2(f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f)));
+    } else {
+      e = f2_pack(ex2_approx(x0), ex2_approx(x1));
+    }
+    l2 = fadd2(l2, e);
+    float e0, e1;
+    f2_unpack(e, e0, e1);
+    pw[i] = pack_bf16x2(e0, e1);
+  }
+}
+
+// Exponentiate the row's scores of one tile from TMEM S into TMEM P, chunk by chunk.
+__device__ __forceinline__ void exp_tile(uint32_t tS, uint32_t tP, bool diag, int kbase, int q_idx, float sl2,
+                                         float m, uint64_t& l2, float& mx) {
+  const uint64_t sc2 = f2_pack(sl2, sl2);
+  const uint64_t nm2 = f2_pack(-m, -m);
+  const bool any_diag = __any_sync(0xffffffffu, diag);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    uint32_t pw[16];
+    tmem_ld32(tS + c, r);
+    tmem_wait_ld();
+    if (any_diag) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (kbase + c + i > q_idx) r[i] = __float_as_uint(-INFINITY);
+      exp_chunk<false>(r, sc2, nm2, l2, mx, pw);
+    } else {
+      exp_chunk<true>(r, sc2, nm2, l2, mx, pw);
+    }
+    tmem_st16(tP + c / 2, pw);
+  }
+}
+
+// Row max of the raw scores of one tile (masked), read from TMEM S.
+__device__ __forceinline__ float max_tile(uint32_t tS, int kbase, int q_idx) {
+  float mx = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(tS + c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (kbase + c + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
+  }
+  return mx;
+}
+
+// Multiply the D fp32 columns of O (this row) by f.
+__device__ __forceinline__ void scale_o(uint32_t tO, float f) {
+#pragma unroll
+  for (int c = 0; c < D; c += 32) {
+    uint32_t o[32];
+    tmem_ld32(tO + c, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+    tmem_st32(tO + c, o);
+  }
+}
+
+// Multiply the 128 bf16 P values of this row (64 columns) by f (a power of two: exact).
+__device__ __forceinline__ void scale_p(uint32_t tP, float f) {
+#pragma unroll
+  for (int c = 0; c < 64; c += 32) {
+    uint32_t w[32];
+    tmem_ld32(tP + c, w);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
+      float2 fv = __bfloat1622float2(v);
+      w[i] = pack_bf16x2(fv.x * f, fv.y * f);
+    }
+    tmem_st32(tP + c, w);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using L = Layout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::BAR + 8 * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // bands of one (batch, head) back to back, heaviest first (K/V reuse in L2)
+  const int n_bands = (p.T + 255) / 256;
+  const int lin = blockIdx.x;
+  const int band = n_bands - 1 - lin % n_bands;
+  const int bh = lin / n_bands;
+  const int b = bh / p.H;
+  const int h = bh % p.H;
+  const int q0 = band * 256;
+  const bool b_live = q0 + 128 < p.T;          // tile B has rows inside the sequence
+  const int nA = 2 * band + 1;                 // KV tiles 0..2*band (diagonal at 2*band)
+  const int nB = b_live ? 2 * band + 2 : 0;    // KV tiles 0..2*band+1 (diagonal at 2*band+1)
+  const int n_kv = b_live ? nB : nA;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B_Q), 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(B_KFULL + s), 1);
+      mbar_init(bar(B_VFULL + s), 1);
+      mbar_init(bar(B_KVEMPTY + s), 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(bar(B_SFULL + w), 1);
+      mbar_init(bar(B_TDONE + w), 128);
+      mbar_init(bar(B_PVDONE + w), 1);
+    }
+    mbar_init(bar(B_FINAL), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(bar(B_Q), (b_live ? 2 : 1) * 128 * D * 2);
+      tma_load_4d(sbase + L::QA, &tmQ, 0, q0, h, b, bar(B_Q));
+      if (b_live) tma_load_4d(sbase + L::QB, &tmQ, 0, q0 + 128, h, b, bar(B_Q));
+      int last_use[NS];
+      for (int s = 0; s < NS; ++s) last_use[s] = -1;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % NS;
+        if (j >= NS) {
+          ok = mbar_wait(bar(B_KVEMPTY + s), ((j / NS) - 1) & 1, abort_flag, 21);
+          if (!ok) break;
+        }
+        mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
+        tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, h, b, bar(B_KFULL + s));
+        mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
+        tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, h, b, bar(B_VFULL + s));
+        last_use[s] = j / NS;
+      }
+      if (!ok || *abort_flag) {
+        volatile int never = 0;
+        mbar_wait(bar(B_Q), 0, &never, 0);
+        for (int s = 0; s < NS; ++s) {
+          if (last_use[s] >= 0) {
+            mbar_wait(bar(B_KFULL + s), last_use[s] & 1, &never, 0);
+            mbar_wait(bar(B_VFULL + s), last_use[s] & 1, &never, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // iteration j: for each tile w, once its softmax finished tile j-1:
+    //   S_w(j) = Q_w K_j^T  (so the softmax can start tile j)  then  O_w += P_w(j-1) V_{j-1}
+    if (lane == 0) {
+      constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
+      constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
+      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, 22);
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        const int s = j % NS;
+        const int s2 = (j + NS - 1) % NS;
+        if (j < n_kv) {
+          ok = mbar_wait(bar(B_KFULL + s), (j / NS) & 1, abort_flag, 23);
+          if (!ok) break;
+        }
+        if (j >= 1) {
+          ok = mbar_wait(bar(B_VFULL + s2), ((j - 1) / NS) & 1, abort_flag, 25);
+          if (!ok) break;
+        }
+        for (int w = 0; w < 2; ++w) {
+          const int nw = (w == 0) ? nA : nB;
+          if (j >= 1 && j - 1 < nw) {
+            ok = mbar_wait(bar(B_TDONE + w), (j - 1) & 1, abort_flag, 24);
+            if (!ok) break;
+          }
+          tc_fence_after();
+          if (j < nw) {
+            const uint32_t qbase = sbase + (w == 0 ? L::QA : L::QB);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t qa = qbase + kk * 32;
+              const uint32_t ka = sbase + L::K + s * kBlockBytes + kk * 32;
+              umma_f16_ss(tmem + kColS + 128 * w, sw128_desc(qa, 16, 1024), sw128_desc(ka, 16, 1024), kIdescS,
+                          kk > 0);
+            }
+            umma_commit(bar(B_SFULL + w));
+          }
+          if (j >= 1 && j - 1 < nw) {
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint32_t va = sbase + L::V + s2 * kBlockBytes + kk * 16 * 128;
+              umma_f16_ts(tmem + kColO + 64 * w, tmem + kColP + 64 * w + kk * 8, sw128_desc(va, kBlockBytes, 1024),
+                          kIdescPV, (j - 1 > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bar(B_PVDONE + w));
+          }
+        }
+        if (!ok) break;
+        if (j >= 1) umma_commit(bar(B_KVEMPTY + s2));
+      }
+      umma_commit(bar(B_FINAL));
+      volatile int never = 0;
+      mbar_wait(bar(B_FINAL), 0, &never, 27);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int w = (warp - 4) >> 2;             // 0: tile A, 1: tile B
+    const int wq = warp & 3;                   // TMEM lane quarter
+    const int row = wq * 32 + lane;
+    const int q_idx = q0 + 128 * w + row;
+    const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + kColS + 128 * w + t_lane;
+    const uint32_t tP = tmem + kColP + 64 * w + t_lane;
+    const uint32_t tO = tmem + kColO + 64 * w + t_lane;
+    const int n_w = (w == 0) ? nA : nB;
+    const float sl2 = p.scale_log2;
+    float m_used = 0.f;                        // reference max (log2 units) of this row
+    uint64_t l2 = f2_pack(0.f, 0.f);
+    bool ok = true;
+    for (int j = 0; j < n_w; ++j) {
+      ok = mbar_wait(bar(B_SFULL + w), j & 1, abort_flag, 28);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      const int kbase = j * BN;
+      const bool diag = kbase + BN - 1 > q_idx;
+      if (j == 0) m_used = max_tile(tS, kbase, q_idx) * sl2;
+      if (j >= 1) {
+        // P columns were read by PV_w(j-1), and O must be complete before any rescale
+        ok = mbar_wait(bar(B_PVDONE + w), (j - 1) & 1, abort_flag, 30);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+      }
+      float mx = -INFINITY;
+      const uint64_t l_before = l2;
+      exp_tile(tS, tP, diag, kbase, q_idx, sl2, m_used, l2, mx);
+      tmem_wait_st();
+      if (__any_sync(0xffffffffu, mx > 120.0f)) {
+        // a score far above the reference max (only with inputs that are not unit q/k, where
+        // 2^x could overflow): redo this tile from its true max -- S is still in TMEM
+        const float m_new = fmaxf(m_used, max_tile(tS, kbase, q_idx) * sl2);
+        const float f = ex2_approx(m_used - m_new);
+        if (j >= 1) scale_o(tO, f);
+        float la, lb;
+        f2_unpack(l_before, la, lb);
+        l2 = f2_pack(la * f, lb * f);
+        float mx2 = -INFINITY;
+        exp_tile(tS, tP, diag, kbase, q_idx, sl2, m_new, l2, mx2);
+        tmem_wait_st();
+        m_used = m_new;
+      } else if (__any_sync(0xffffffffu, mx > 8.0f)) {
+        // raise the reference max by an integer k so every 2^x <= 2^8: P, O and l scale by 2^-k (exact)
+        const float k = mx > 8.0f ? ceilf(mx) - 8.0f : 0.0f;   // integer in [0, 112]
+        const float f = __int_as_float((127 - (int)k) << 23);    // exactly 2^-k
+        scale_p(tP, f);
+        if (j >= 1) scale_o(tO, f);
+        tmem_wait_st();
+        float la, lb;
+        f2_unpack(l2, la, lb);
+        l2 = f2_pack(la * f, lb * f);
+        m_used += k;
+      }
+      tc_fence_before();
+      mbar_arrive(bar(B_TDONE + w));
+    }
+    if (ok && n_w > 0) {
+      ok = mbar_wait(bar(B_PVDONE + w), (n_w - 1) & 1, abort_flag, 31);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        float la, lb;
+        f2_unpack(l2, la, lb);
+        const float inv_l = 1.0f / (la + lb);
+        __nv_bfloat16* orow = p.o + (int64_t)b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)h * p.os_h;
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tO + c, o);
+          tmem_wait_ld();
+          if (q_idx < p.T) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+              v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+              v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+              v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + c + i) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace v2
+
 // --------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -363,6 +748,32 @@ static bool tc_eligible(const void* q, const void* k, const void* v, void* o, in
   for (int i = 0; i < 12; ++i)
     if ((s[i] * 2) % 16 != 0 || s[i] <= 0) return false;
   return true;
+}
+
+static int launch_v2(const void* q, const void* k, const void* v, void* o, int B, int T, int H, float scale,
+                     const int64_t* s, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, q, 64, T, H, B, s[1], s[2], s[0]))) return rc;
+  if ((rc = make_map(&mk, k, 64, T, H, B, s[4], s[5], s[3]))) return rc;
+  if ((rc = make_map(&mv, v, 64, T, H, B, s[7], s[8], s[6]))) return rc;
+  Params p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.os_b = s[9];
+  p.os_t = s[10];
+  p.os_h = s[11];
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.n_qt = (T + 255) / 256;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t blocks = (int64_t)p.n_qt * B * H;
+  ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
+  cudaError_t e = cudaFuncSetAttribute(v2::attn_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       v2::Layout::kDynSmem);
+  if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "attention: smem attribute: %s", cudaGetErrorString(e));
+  v2::attn_fwd2_kernel<<<(unsigned)blocks, v2::kThreads, v2::Layout::kDynSmem, st>>>(mq, mk, mv, p);
+  return check_launch("attention (tcgen05, 2-tile)");
 }
 
 template <int D>
@@ -403,18 +814,22 @@ extern "C" int engpt_causal_attention(const void* q, const void* k, const void* 
   clear_error();
   ENGPT_REQUIRE(B >= 0 && T >= 0 && H > 0 && Dh > 0, ENGPT_ERR_SHAPE, "attention: B=%d T=%d H=%d Dh=%d", B, T, H, Dh);
   ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "attention: dtype %d", dtype);
-  ENGPT_REQUIRE(impl >= ENGPT_ATTN_AUTO && impl <= ENGPT_ATTN_SIMT, ENGPT_ERR_ARG, "attention: impl %d", impl);
+  ENGPT_REQUIRE(impl >= ENGPT_ATTN_AUTO && impl <= ENGPT_ATTN_TCGEN05_1TILE, ENGPT_ERR_ARG, "attention: impl %d",
+                impl);
   if ((int64_t)B * T == 0) return ENGPT_OK;
   ENGPT_REQUIRE(q && k && v && o && strides, ENGPT_ERR_ARG, "attention: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool tc_ok = dtype == ENGPT_BF16 && attn_tc::tc_eligible(q, k, v, o, Dh, strides);
-  if (impl == ENGPT_ATTN_TCGEN05 && !tc_ok)
+  if ((impl == ENGPT_ATTN_TCGEN05 || impl == ENGPT_ATTN_TCGEN05_1TILE) && !tc_ok)
     return set_error(ENGPT_ERR_UNSUPPORTED,
                      "attention: tcgen05 kernel needs bf16, head_dim 64/128 and 16-byte aligned rows (Dh=%d)", Dh);
   if (tc_ok && impl != ENGPT_ATTN_SIMT) {
     int rc = attn_tc::get_encode();
     if (rc) return rc;
-    if (Dh == 64) return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, st);
+    if (Dh == 64) {
+      if (impl == ENGPT_ATTN_TCGEN05_1TILE) return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, st);
+      return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, st);
+    }
     return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, st);
   }
   return launch_attn_simt(q, k, v, o, dtype, B, T, H, Dh, scale, strides, st);

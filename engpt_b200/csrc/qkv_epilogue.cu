@@ -31,11 +31,13 @@ struct QkvArgs {
   int layout;  // 0: [B,T,H,Dh], 1: [B,H,T,Dh]
 };
 
+// token index n < 2^31 (checked on the host), so the split into (b, t) is 32-bit
 __device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t n, int h) {
   if (a.layout == 0) return (n * a.H + h) * (int64_t)a.Dh;
-  const int64_t b = n / a.T;
-  const int64_t t = n - b * a.T;
-  return ((b * a.H + h) * (int64_t)a.T + t) * a.Dh;
+  const int ni = (int)n;
+  const int b = ni / a.T;
+  const int t = ni - b * a.T;
+  return ((int64_t)(b * a.H + h) * a.T + t) * a.Dh;
 }
 
 template <typename T>
@@ -63,37 +65,29 @@ __device__ __forceinline__ void store8<float>(float* p, const float* x) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
 }
 
-// LPR lanes per row (Dh = 8 * LPR), LPR divides 32.
+// One CTA per token: thread e8 of the 3*d/8 threads owns 8 consecutive
+// elements of the token's [3, H, Dh] slice, i.e. (s, h, sub) with LPR lanes
+// (Dh = 8 * LPR, LPR divides 32) per (s, h) row.
 template <typename T, int LPR>
-__global__ void __launch_bounds__(256) qkv_vec_kernel(QkvArgs a) {
-  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t task = gid / LPR;
-  const int sub = (int)(gid % LPR);
-  const int64_t ntask = (int64_t)a.B * a.T * 3 * a.H;
-  const bool live = task < ntask;
-  // task = (n * 3 + s) * H + h
-  const int64_t tt = live ? task : 0;
-  const int h = (int)(tt % a.H);
-  const int64_t ns = tt / a.H;
-  const int s = (int)(ns % 3);
-  const int64_t n = ns / 3;
+__global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
+  const int64_t n = blockIdx.x;                   // token = b * T + t
+  const int e8 = threadIdx.x;                     // < 3 * H * LPR
+  const int row = e8 / LPR;                       // s * H + h
+  const int sub = e8 - row * LPR;
+  const int s = row / a.H;
+  const int h = row - s * a.H;
   const int e0 = sub * 8;
-  const T* src = reinterpret_cast<const T*>(a.qkv) + tt * (int64_t)a.Dh + e0;
+  const T* src = reinterpret_cast<const T*>(a.qkv) + (n * 3 * a.H + row) * (int64_t)a.Dh + e0;
 
   float x[8];
-  if (live) load8<T>(src, x);
-  else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.f;
-  }
-  const float rho = live ? a.rho[n] : 1.f;
+  load8<T>(src, x);
+  const float rho = a.rho[n];
   // sum of squares across the LPR lanes of this row (groups are lane-aligned)
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
   for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (!live) return;
 
   float outv[8];
   if (s == 2) {
@@ -102,7 +96,7 @@ __global__ void __launch_bounds__(256) qkv_vec_kernel(QkvArgs a) {
   } else {
     float den = sqrtf(ss);
     if (a.eps > 0.f) den = fmaxf(den, rho * a.eps);
-    const int t = (int)(n % a.T);
+    const int t = (int)n - ((int)n / a.T) * a.T;
     const int p0 = e0 >> 1;  // first pair index of this lane
     float c[4], sn[4];
     if ((a.rope_half & 3) == 0 && p0 + 4 <= a.rope_half) {
@@ -223,15 +217,17 @@ extern "C" int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rh
                       aligned(qkv, 16) && aligned(q_out, 16) && aligned(k_out, 16) && aligned(v_out, 16) &&
                       aligned(qk_scale, 16) && (rope_half == 0 || (aligned(cos_tab, 16) && aligned(sin_tab, 16))) &&
                       ((int64_t)Dh * esz) % 16 == 0;
-  if (vec_ok) {
+  const int threads_per_token = 3 * H * (Dh / 8);
+  if (vec_ok && threads_per_token <= 768 && threads_per_token % 32 == 0) {
     const int lpr = Dh / 8;
-    const int64_t threads = ntask * lpr;
-    const int64_t blocks = (threads + 255) / 256;
+    const int64_t blocks = (int64_t)B * T;
     ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "qkv_postprocess: too large");
-#define ENGPT_QKV_LAUNCH(L)                                                                           \
-  case L:                                                                                             \
-    if (dtype == ENGPT_BF16) qkv_vec_kernel<__nv_bfloat16, L><<<(unsigned)blocks, 256, 0, st>>>(a);    \
-    else qkv_vec_kernel<float, L><<<(unsigned)blocks, 256, 0, st>>>(a);                               \
+#define ENGPT_QKV_LAUNCH(L)                                                                                  \
+  case L:                                                                                                    \
+    if (dtype == ENGPT_BF16)                                                                                 \
+      qkv_vec_kernel<__nv_bfloat16, L><<<(unsigned)blocks, threads_per_token, 0, st>>>(a);                   \
+    else                                                                                                     \
+      qkv_vec_kernel<float, L><<<(unsigned)blocks, threads_per_token, 0, st>>>(a);                           \
     break;
     switch (lpr) {
       ENGPT_QKV_LAUNCH(1)

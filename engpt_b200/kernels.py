@@ -165,7 +165,8 @@ def causal_sdpa(q: Tensor, k: Tensor, v: Tensor, *, scale: float, dropout_p: flo
     q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
     o = torch.empty(bsz, seq_len, n_head, head_dim, device=q.device, dtype=q.dtype)
     strides = attention_strides(q, k, v, o, head_major=False)
-    code = {"auto": _lib.ATTN_AUTO, "tcgen05": _lib.ATTN_TCGEN05, "simt": _lib.ATTN_SIMT}[impl]
+    code = {"auto": _lib.ATTN_AUTO, "tcgen05": _lib.ATTN_TCGEN05, "simt": _lib.ATTN_SIMT,
+            "tcgen05_1tile": _lib.ATTN_TCGEN05_1TILE}[impl]
     with torch.cuda.device(q.device):
         causal_attention_into(q, k, v, o, scale, strides, bsz, seq_len, n_head, head_dim, code)
     return o

@@ -156,7 +156,11 @@ class _Workspace:
             self.w = [dict(qkv=e(3 * d, d), out=e(d, d), ug=e(2 * W, d), down=e(d, W)) for _ in range(cfg.n_layer)]
         else:
             self.w = None
-        self.w_head = e(cfg.vocab_size, d)
+        # output-head weight with the vocab rounded up to a multiple of 64 rows (pad rows stay zero):
+        # an odd vocab (50257) would give the logits GEMM an unaligned leading dimension, which
+        # sends cuBLAS to a ~10x slower kernel
+        self.vocab_pad = -(-cfg.vocab_size // 64) * 64
+        self.w_head = torch.zeros(self.vocab_pad, d, device=device, dtype=act)
 
 
 class EfficientNGPT(nn.Module):
@@ -177,6 +181,9 @@ class EfficientNGPT(nn.Module):
         self.project_parameters_()
         self._ws: Optional[_Workspace] = None
         self.attn_impl = _lib.ATTN_AUTO
+        # False: logits are a strided [B, T, V] view of a [N, V rounded up to 64] buffer (no copy);
+        # True: a contiguous copy is returned
+        self.contiguous_logits = False
         # optional instrumentation: called around the attention launch of every layer
         self.attn_timer: Optional[Callable[[str], None]] = None
 
@@ -353,18 +360,21 @@ class EfficientNGPT(nn.Module):
             # output head (engpt/kernels.py:209-229 with logit_scale, engpt/models.py:366-368)
             _lib.call("engpt_scale_rows_cast", self.output_emb.data_ptr(), self.s_z.data_ptr(),
                       float(self.logit_mult), cfg.vocab_size, d, ws.w_head.data_ptr(), act, st)
-            logits = torch.empty(bsz, seq_len, cfg.vocab_size, device=dev, dtype=ws.act)
-            x_head = ws.x if len(self.blocks) > 0 else None
-            if x_head is None:
-                raise ValueError("n_layer must be positive")
-            torch.mm(x_head, ws.w_head.t(), out=logits.view(n, cfg.vocab_size))
+            # logits are computed into a [N, V_pad] buffer and returned as the [B, T, V] view of its
+            # first V columns (row stride V_pad); values are those of the [N, V] product
+            vp = ws.vocab_pad
+            logits_buf = torch.empty(n, vp, device=dev, dtype=ws.act)
+            torch.mm(ws.x, ws.w_head.t(), out=logits_buf)
+            logits = logits_buf.view(bsz, seq_len, vp)[:, :, :cfg.vocab_size]
+            if self.contiguous_logits:
+                logits = logits.contiguous()
             loss = None
             if targets is not None:
                 if targets.ndim != 2:
                     raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
                 t = targets.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
                 loss = torch.empty((), device=dev, dtype=torch.float32)
-                _lib.call("engpt_cross_entropy", logits.data_ptr(), act, n, cfg.vocab_size, cfg.vocab_size,
+                _lib.call("engpt_cross_entropy", logits_buf.data_ptr(), act, n, cfg.vocab_size, vp,
                           t.data_ptr(), ws.row_loss.data_ptr(), loss.data_ptr(), st)
         return logits, loss
 

@@ -57,7 +57,8 @@ enum engpt_aux_mode {
 enum engpt_attn_impl {
   ENGPT_ATTN_AUTO = 0,   /* tcgen05 kernel when bf16 and head_dim in {64,128}, else SIMT */
   ENGPT_ATTN_TCGEN05 = 1,
-  ENGPT_ATTN_SIMT = 2
+  ENGPT_ATTN_SIMT = 2,
+  ENGPT_ATTN_TCGEN05_1TILE = 3  /* tcgen05 kernel with one 128-query tile per CTA (head_dim 64 comparison path) */
 };
 
 /* Message for the last failing call on this host thread ("" if none). */

@@ -173,6 +173,32 @@ def test_attention_tcgen05_head_major_strides_and_unnormalised_inputs(cuda, D):
     np.testing.assert_allclose(o.float().cpu().numpy(), ref, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("T", [130, 700])
+def test_attention_tcgen05_one_tile_variant_vs_oracle(cuda, T):
+    """The one-128-query-tile-per-CTA kernel (head_dim 64 comparison path)."""
+    q, k, v = _attn_inputs(2, T, 2, 64, seed=T)
+    qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
+    o = K.causal_sdpa(qb, kb, vb, scale=8.0, dropout_p=0.0, impl="tcgen05_1tile")
+    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), 8.0)
+    assert np.abs(o.float().cpu().numpy() - ref).max() < 1.5e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_tcgen05_score_jumps(cuda, D):
+    """Scores that jump far above the running reference max mid-sequence (exercises the O/P rescale
+    and the tile-restart paths of the kernel): keys at a few positions are large multiples of a query."""
+    B, T, H = 1, 600, 2
+    q, k, v = _attn_inputs(B, T, H, D, seed=99, normalize=False)
+    for pos, mult in ((5, 4.0), (300, 30.0), (450, 200.0)):
+        k[:, pos] = q[:, pos + 3] * mult
+    qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
+    scale = 1.0 / math.sqrt(D)
+    o = K.causal_sdpa(qb, kb, vb, scale=scale, dropout_p=0.0, impl="tcgen05")
+    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), scale)
+    assert np.isfinite(o.float().cpu().numpy()).all()
+    np.testing.assert_allclose(o.float().cpu().numpy(), ref, atol=2e-2, rtol=2e-2)
+
+
 def test_attention_simt_bf16_odd_head_dim(cuda):
     q, k, v = _attn_inputs(2, 77, 2, 24, seed=3)
     qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
