@@ -383,6 +383,7 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
         "engpt_swiglu": (4 + 2) * n * 4 * d,                              # ug bf16 in (2W), out bf16 (W)
         "engpt_cross_entropy": 2 * n * a.vocab + 12 * n,
         "engpt_embed_carried": (4 + 4 + 2) * n * d + 12 * n,
+        "engpt_cast_f32_bf16_many": 6 * 16 * a.layers * d * d,            # fp32 weights in, bf16 out
     }
     out = {}
     for name, evs in per.items():

@@ -22,6 +22,7 @@ OK = 0
 STATUS_NAMES = {1: "shape", 2: "dtype", 3: "alignment", 4: "launch", 5: "device timeout", 6: "unsupported",
                 7: "argument"}
 AUX_NONE, AUX_BF16_Y, AUX_BF16_H, AUX_F32_H = 0, 1, 2, 3
+QKV_BTHD, QKV_BHTD, QKV_INPLACE = 0, 1, 2
 ATTN_AUTO, ATTN_TCGEN05, ATTN_SIMT, ATTN_TCGEN05_1TILE = 0, 1, 2, 3
 
 _lock = threading.Lock()
@@ -44,6 +45,7 @@ SIGNATURES = {
     "engpt_embed_carried": (_i, [_p, _p, _i64, _i, _i64, _p, _p, _p, _p]),
     "engpt_swiglu": (_i, [_p, _i, _p, _p, _f, _f, _i64, _i, _p, _i, _p]),
     "engpt_scale_rows_cast": (_i, [_p, _p, _f, _i64, _i64, _p, _i, _p]),
+    "engpt_cast_f32_bf16_many": (_i, [_p, _p, _p, _i, _p]),
     "engpt_cross_entropy": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _p]),
     "engpt_cross_entropy_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
 }

@@ -99,37 +99,61 @@ __global__ void embed_kernel(const int64_t* __restrict__ idx, const float* __res
 // ------------------------------------------------------------ SwiGLU epilogue
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+// SiLU on the hot path: MUFU exp and approximate reciprocal (a few ulp in
+// fp32, far below the bf16 rounding of the result).  For x -> -inf the
+// denominator overflows and __fdividef returns 0, the limit of x*sigmoid(x).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ float load_as_f32(const float* p, int64_t i) { return p[i]; }
 __device__ __forceinline__ float load_as_f32(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
 __device__ __forceinline__ void store_f32(float* p, int64_t i, float v) { p[i] = v; }
 __device__ __forceinline__ void store_f32(__nv_bfloat16* p, int64_t i, float v) { p[i] = __float2bfloat16_rn(v); }
 
-// Vector path: bf16 in, bf16 out, width % 8 == 0.  8 output columns per thread.
-__global__ void swiglu_bf16_vec_kernel(const __nv_bfloat16* __restrict__ ug, const float* __restrict__ s_u,
-                                       const float* __restrict__ s_gate, float u_mult, float gate_mult,
-                                       int64_t rows, int width, __nv_bfloat16* __restrict__ out) {
-  int chunks = width >> 3;
-  int64_t total = rows * chunks;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = e / chunks;
-    int c = (int)(e - r * chunks) << 3;
-    const __nv_bfloat16* row = ug + r * (int64_t)(2 * width);
-    float u[8], g[8], o[8];
-    unpack8(ld_stream(row + c), u);
-    unpack8(ld_stream(row + width + c), g);
+// Vector path: bf16 in, bf16 out, width % 8 == 0.  A block owns whole rows
+// (blockIdx.x: row group, threads: 8-column chunks); each thread keeps
+// kSwiRows rows' loads in flight before computing.
+constexpr int kSwiRows = 4;
+
+__global__ void __launch_bounds__(256, 3) swiglu_bf16_vec_kernel(const __nv_bfloat16* __restrict__ ug,
+                                                                 const float* __restrict__ s_u,
+                                                                 const float* __restrict__ s_gate, float u_mult,
+                                                                 float gate_mult, int64_t rows, int width,
+                                                                 __nv_bfloat16* __restrict__ out) {
+  const int chunks = width >> 3;
+  for (int ch = threadIdx.x; ch < chunks; ch += blockDim.x) {
+    const int c = ch << 3;
     float4 su0 = *reinterpret_cast<const float4*>(s_u + c);
     float4 su1 = *reinterpret_cast<const float4*>(s_u + c + 4);
     float4 sg0 = *reinterpret_cast<const float4*>(s_gate + c);
     float4 sg1 = *reinterpret_cast<const float4*>(s_gate + c + 4);
-    float su[8] = {su0.x, su0.y, su0.z, su0.w, su1.x, su1.y, su1.z, su1.w};
-    float sg[8] = {sg0.x, sg0.y, sg0.z, sg0.w, sg1.x, sg1.y, sg1.z, sg1.w};
+    const float su[8] = {su0.x, su0.y, su0.z, su0.w, su1.x, su1.y, su1.z, su1.w};
+    const float sg[8] = {sg0.x, sg0.y, sg0.z, sg0.w, sg1.x, sg1.y, sg1.z, sg1.w};
+    for (int64_t r0 = (int64_t)blockIdx.x * kSwiRows; r0 < rows; r0 += (int64_t)gridDim.x * kSwiRows) {
+      uint4 ru[kSwiRows], rg[kSwiRows];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float uu = (u[i] * su[i]) * u_mult;
-      float gg = (g[i] * sg[i]) * gate_mult;
-      o[i] = uu * silu_f(gg);
+      for (int k = 0; k < kSwiRows; ++k) {
+        if (r0 + k < rows) {
+          const __nv_bfloat16* row = ug + (r0 + k) * (int64_t)(2 * width);
+          ru[k] = ld_stream(row + c);
+          rg[k] = ld_stream(row + width + c);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kSwiRows; ++k) {
+        if (r0 + k < rows) {
+          float u[8], g[8], o[8];
+          unpack8(ru[k], u);
+          unpack8(rg[k], g);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float uu = (u[i] * su[i]) * u_mult;
+            const float gg = (g[i] * sg[i]) * gate_mult;
+            o[i] = uu * silu_fast(gg);
+          }
+          st_stream(out + (r0 + k) * (int64_t)width + c, pack8(o));
+        }
+      }
     }
-    st_stream(out + r * (int64_t)width + c, pack8(o));
   }
 }
 
@@ -176,6 +200,37 @@ __global__ void scale_rows_cast_bf16_vec_kernel(const float* __restrict__ src, c
       for (int i = 0; i < 8; ++i) v[i] = v[i] * s;
     }
     *reinterpret_cast<uint4*>(out + base) = pack8(v);
+  }
+}
+
+// ---------------------------------------------------- batched fp32->bf16 cast
+constexpr int kCastMax = 64;
+struct CastList {
+  const float* src[kCastMax];
+  __nv_bfloat16* dst[kCastMax];
+  int64_t count[kCastMax];
+};
+
+// grid.y = tensor, grid.x strides over that tensor in 8-element chunks
+__global__ void __launch_bounds__(256) cast_many_kernel(const __grid_constant__ CastList L) {
+  const int t = blockIdx.y;
+  const float* __restrict__ src = L.src[t];
+  __nv_bfloat16* __restrict__ dst = L.dst[t];
+  const int64_t n = L.count[t];
+  const int64_t n8 = n / 8;
+  const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (vec) {
+    for (int64_t e = first; e < n8; e += stride) {
+      float4 a = *reinterpret_cast<const float4*>(src + e * 8);
+      float4 b = *reinterpret_cast<const float4*>(src + e * 8 + 4);
+      float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      *reinterpret_cast<uint4*>(dst + e * 8) = pack8(v);
+    }
+    for (int64_t e = n8 * 8 + first; e < n; e += stride) dst[e] = __float2bfloat16_rn(src[e]);
+  } else {
+    for (int64_t e = first; e < n; e += stride) dst[e] = __float2bfloat16_rn(src[e]);
   }
 }
 
@@ -358,8 +413,12 @@ int engpt_swiglu(const void* ug, int dtype, const float* s_u, const float* s_gat
   cudaStream_t st = as_stream(stream);
   if (dtype == ENGPT_BF16 && out_dtype == ENGPT_BF16 && (width % 8) == 0 && aligned(ug, 16) && aligned(out, 16) &&
       aligned(s_u, 16) && aligned(s_gate, 16)) {
-    swiglu_bf16_vec_kernel<<<grid_for(rows * (width / 8), 256), 256, 0, st>>>(
-        (const __nv_bfloat16*)ug, s_u, s_gate, u_mult, gate_mult, rows, width, (__nv_bfloat16*)out);
+    const int64_t groups = (rows + kSwiRows - 1) / kSwiRows;
+    const int threads = (width / 8) < 256 ? (((width / 8) + 31) / 32) * 32 : 256;
+    const int64_t cap = (int64_t)num_sms() * 8 * (256 / threads);
+    const int blocks = (int)(groups < cap ? groups : cap);
+    swiglu_bf16_vec_kernel<<<blocks, threads, 0, st>>>((const __nv_bfloat16*)ug, s_u, s_gate, u_mult, gate_mult,
+                                                        rows, width, (__nv_bfloat16*)out);
   } else if (dtype == ENGPT_BF16 && out_dtype == ENGPT_BF16) {
     swiglu_generic_kernel<__nv_bfloat16, __nv_bfloat16><<<grid_for(rows * width, 256), 256, 0, st>>>(
         (const __nv_bfloat16*)ug, s_u, s_gate, u_mult, gate_mult, rows, width, (__nv_bfloat16*)out);
@@ -398,6 +457,43 @@ int engpt_scale_rows_cast(const float* src, const float* scale, float mult, int6
     return set_error(ENGPT_ERR_DTYPE, "scale_rows_cast: out dtype %d", out_dtype);
   }
   return check_launch("scale_rows_cast");
+}
+
+int engpt_cast_f32_bf16_many(const void* const* src, void* const* dst, const int64_t* counts, int n,
+                             void* stream) {
+  clear_error();
+  ENGPT_REQUIRE(n >= 0, ENGPT_ERR_SHAPE, "cast_many: n=%d", n);
+  if (n == 0) return ENGPT_OK;
+  ENGPT_REQUIRE(src && dst && counts, ENGPT_ERR_ARG, "cast_many: null pointer array");
+  cudaStream_t st = as_stream(stream);
+  for (int base = 0; base < n; base += kCastMax) {
+    const int m = (n - base) < kCastMax ? (n - base) : kCastMax;
+    CastList L;
+    int64_t maxc = 0;
+    for (int i = 0; i < m; ++i) {
+      ENGPT_REQUIRE(counts[base + i] >= 0, ENGPT_ERR_SHAPE, "cast_many: count[%d] < 0", base + i);
+      ENGPT_REQUIRE(counts[base + i] == 0 || (src[base + i] && dst[base + i]), ENGPT_ERR_ARG,
+                    "cast_many: null tensor %d", base + i);
+      L.src[i] = static_cast<const float*>(src[base + i]);
+      L.dst[i] = static_cast<__nv_bfloat16*>(dst[base + i]);
+      L.count[i] = counts[base + i];
+      if (L.count[i] > maxc) maxc = L.count[i];
+    }
+    for (int i = m; i < kCastMax; ++i) {
+      L.src[i] = nullptr;
+      L.dst[i] = nullptr;
+      L.count[i] = 0;
+    }
+    // enough blocks per tensor to fill the GPU with the whole batch in flight
+    int64_t per = (maxc / 8 + 255) / 256;
+    const int64_t cap = ((int64_t)num_sms() * 8 + m - 1) / m;
+    if (per > cap) per = cap;
+    if (per < 1) per = 1;
+    cast_many_kernel<<<dim3((unsigned)per, (unsigned)m), 256, 0, st>>>(L);
+    int rc = check_launch("cast_f32_bf16_many");
+    if (rc) return rc;
+  }
+  return ENGPT_OK;
 }
 
 int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t ld,

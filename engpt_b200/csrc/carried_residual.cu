@@ -40,10 +40,12 @@ __device__ __forceinline__ float eff_alpha(const ResidualArgs& a, float raw) {
 }
 
 struct RowScalars {
-  float coef_y;  // c_b (gauge folded in at write time)
-  float coef_b;  // rho
-  float g;       // gauge divisor (1 when inactive)
+  float coef_y;   // c_b (gauge folded in at write time)
+  float coef_b;   // rho
+  float g;        // gauge divisor (1 when inactive)
+  float inv_g;    // 1 / g
   float rho_new;
+  float inv_rho;  // 1 / rho_new, for the Y/rho side output
 };
 
 __device__ __forceinline__ RowScalars finish_row(const ResidualArgs& a, float rho, float r0, float r1, float r2,
@@ -60,20 +62,23 @@ __device__ __forceinline__ RowScalars finish_row(const ResidualArgs& a, float rh
   s.coef_y = cb;
   s.coef_b = rho;
   s.g = g;
+  s.inv_g = 1.0f / g;
   s.rho_new = (g == 1.0f) ? rho_plus : rho_plus / g;
+  s.inv_rho = 1.0f / s.rho_new;
   return s;
 }
 
+// u / g, with the per-row reciprocal (exact when the gauge is inactive, within 1 ulp otherwise)
 __device__ __forceinline__ float out_value(float alpha, float y, float b, const RowScalars& s) {
   float beta = 1.0f - alpha;
   float u = beta * s.coef_y * y + alpha * s.coef_b * b;
-  return (s.g == 1.0f) ? u : u / s.g;
+  return u * s.inv_g;
 }
 
 // Vector path: d % 8 == 0, d <= 256 * MAXCH.  Lane owns 8-column chunks
 // (lane, lane + 32, ...).  BT = branch element type.
 template <int MAXCH, typename BT>
-__global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
+__global__ void __launch_bounds__(256, (MAXCH <= 4 ? 3 : 1)) residual_vec_kernel(ResidualArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= a.rows) return;
@@ -81,8 +86,11 @@ __global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
   const float* yrow = a.y + row * a.d;
   const BT* brow = reinterpret_cast<const BT*>(a.branch) + row * a.d;
 
+  // the whole row is loaded before any use: Y as fp32, the branch kept in its
+  // storage type (bf16 stays packed, 4 registers per 8 values)
+  constexpr int BW = sizeof(BT) == 2 ? 4 : 8;  // 32-bit words per 8 branch values
   float yv[MAXCH][8];
-  float bv[MAXCH][8];
+  uint32_t bw[MAXCH][BW];
   float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
 #pragma unroll
   for (int k = 0; k < MAXCH; ++k) {
@@ -94,15 +102,24 @@ __global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
       yv[k][0] = y0.x; yv[k][1] = y0.y; yv[k][2] = y0.z; yv[k][3] = y0.w;
       yv[k][4] = y1.x; yv[k][5] = y1.y; yv[k][6] = y1.z; yv[k][7] = y1.w;
       if constexpr (sizeof(BT) == 2) {
-        unpack8(ld_stream(brow + c), bv[k]);
+        uint4 raw = ld_stream(brow + c);
+        bw[k][0] = raw.x; bw[k][1] = raw.y; bw[k][2] = raw.z; bw[k][3] = raw.w;
       } else {
-        float4 b0 = *reinterpret_cast<const float4*>(brow + c);
-        float4 b1 = *reinterpret_cast<const float4*>(brow + c + 4);
-        bv[k][0] = b0.x; bv[k][1] = b0.y; bv[k][2] = b0.z; bv[k][3] = b0.w;
-        bv[k][4] = b1.x; bv[k][5] = b1.y; bv[k][6] = b1.z; bv[k][7] = b1.w;
+        uint4 b0 = *reinterpret_cast<const uint4*>(brow + c);
+        uint4 b1 = *reinterpret_cast<const uint4*>(brow + c + 4);
+        bw[k][0] = b0.x; bw[k][1] = b0.y; bw[k][2] = b0.z; bw[k][3] = b0.w;
+        bw[k][4] = b1.x; bw[k][5] = b1.y; bw[k][6] = b1.z; bw[k][7] = b1.w;
       }
     }
   }
+  auto bval = [&](int k, int i) -> float {
+    if constexpr (sizeof(BT) == 2) {
+      const uint32_t w = bw[k][i >> 1];
+      return __uint_as_float((i & 1) ? (w & 0xffff0000u) : (w << 16));
+    } else {
+      return __uint_as_float(bw[k][i]);
+    }
+  };
 #pragma unroll
   for (int k = 0; k < MAXCH; ++k) {
     const int ch = k * 32 + lane;
@@ -115,7 +132,7 @@ __global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
       for (int i = 0; i < 8; ++i) {
         float alpha = eff_alpha(a, al[i]);
         float beta = 1.0f - alpha;
-        float y = yv[k][i], b = bv[k][i];
+        float y = yv[k][i], b = bval(k, i);
         float bsq = b * b;
         r0 += bsq;
         r1 += (beta * beta) * (y * y);
@@ -141,7 +158,7 @@ __global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
       float al[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = out_value(eff_alpha(a, al[i]), yv[k][i], bv[k][i], s);
+      for (int i = 0; i < 8; ++i) o[i] = out_value(eff_alpha(a, al[i]), yv[k][i], bval(k, i), s);
       *reinterpret_cast<float4*>(yo + c) = make_float4(o[0], o[1], o[2], o[3]);
       *reinterpret_cast<float4*>(yo + c + 4) = make_float4(o[4], o[5], o[6], o[7]);
       if (a.aux_mode == ENGPT_AUX_BF16_Y) {
@@ -149,7 +166,7 @@ __global__ void __launch_bounds__(256) residual_vec_kernel(ResidualArgs a) {
       } else if (a.aux_mode == ENGPT_AUX_BF16_H || a.aux_mode == ENGPT_AUX_F32_H) {
         float h[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) h[i] = o[i] / s.rho_new;
+        for (int i = 0; i < 8; ++i) h[i] = o[i] * s.inv_rho;
         if (a.aux_mode == ENGPT_AUX_BF16_H) {
           st_stream(reinterpret_cast<__nv_bfloat16*>(a.aux) + row * a.d + c, pack8(h));
         } else {
@@ -170,9 +187,8 @@ __device__ __forceinline__ float ld_branch(const void* p, int bt, int64_t i) {
 
 // Generic path: any d.  One warp per row, two strided passes (the second
 // re-reads the row, which stays in L1/L2 for the row sizes this serves).
-// Not used in place: the host routes aliasing calls with d > 2048 or
-// d % 8 != 0 through a copy-free order (reads complete before writes per
-// element, and each element is written by the lane that read it).
+// In-place safe: every element is read in both passes by the lane that
+// writes it, and the first pass ends (warp reduction) before any write.
 __global__ void __launch_bounds__(256) residual_generic_kernel(ResidualArgs a, int bt) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -202,9 +218,9 @@ __global__ void __launch_bounds__(256) residual_generic_kernel(ResidualArgs a, i
     if (a.aux_mode == ENGPT_AUX_BF16_Y) {
       reinterpret_cast<__nv_bfloat16*>(a.aux)[row * a.d + c] = __float2bfloat16_rn(o);
     } else if (a.aux_mode == ENGPT_AUX_BF16_H) {
-      reinterpret_cast<__nv_bfloat16*>(a.aux)[row * a.d + c] = __float2bfloat16_rn(o / s.rho_new);
+      reinterpret_cast<__nv_bfloat16*>(a.aux)[row * a.d + c] = __float2bfloat16_rn(o * s.inv_rho);
     } else if (a.aux_mode == ENGPT_AUX_F32_H) {
-      reinterpret_cast<float*>(a.aux)[row * a.d + c] = o / s.rho_new;
+      reinterpret_cast<float*>(a.aux)[row * a.d + c] = o * s.inv_rho;
     }
   }
   if (lane == 0) a.rho_out[row] = s.rho_new;

@@ -76,6 +76,14 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return r;
 }
 
+// 16-byte load through the coherent path (for buffers the same kernel also writes), not kept in L1.
+__device__ __forceinline__ uint4 ld_once(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
 __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
   asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");

@@ -9,8 +9,9 @@
 // divides, multiplies); here a group of Dh/8 lanes owns one (token, q|k|v,
 // head) row: 16-byte loads, an fp32 sum of squares reduced with shuffles, the
 // rotation on register pairs and one 16-byte store per lane.  Outputs go to
-// [B,T,H,Dh] or directly to the head-major [B,H,T,Dh] layout the attention
-// kernel's TMA reads, so no transpose pass follows.
+// [B,T,H,Dh], to the head-major [B,H,T,Dh], or back over qkv itself
+// ([B,T,3,H,Dh], as the reference's no-grad path does), which the attention
+// kernel's TMA reads through strided tensor maps.
 #include "common.cuh"
 
 namespace engpt {
@@ -28,12 +29,14 @@ struct QkvArgs {
   void* q;
   void* k;
   void* v;
-  int layout;  // 0: [B,T,H,Dh], 1: [B,H,T,Dh]
+  int layout;  // ENGPT_QKV_BTHD, ENGPT_QKV_BHTD or ENGPT_QKV_INPLACE
 };
 
-// token index n < 2^31 (checked on the host), so the split into (b, t) is 32-bit
-__device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t n, int h) {
-  if (a.layout == 0) return (n * a.H + h) * (int64_t)a.Dh;
+// Element offset of row (token n, part s, head h) in the output of part s.
+// Token index n < 2^31 (checked on the host), so the (b, t) split is 32-bit.
+__device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t n, int s, int h) {
+  if (a.layout == ENGPT_QKV_INPLACE) return ((n * 3 + s) * a.H + h) * (int64_t)a.Dh;
+  if (a.layout == ENGPT_QKV_BTHD) return (n * a.H + h) * (int64_t)a.Dh;
   const int ni = (int)n;
   const int b = ni / a.T;
   const int t = ni - b * a.T;
@@ -44,7 +47,7 @@ template <typename T>
 __device__ __forceinline__ void load8(const T* p, float* x);
 template <>
 __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* x) {
-  unpack8(ld_stream(p), x);
+  unpack8(ld_once(p), x);  // coherent load: the output may be written over qkv in place
 }
 template <>
 __device__ __forceinline__ void load8<float>(const float* p, float* x) {
@@ -65,74 +68,101 @@ __device__ __forceinline__ void store8<float>(float* p, const float* x) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
 }
 
-// One CTA per token: thread e8 of the 3*d/8 threads owns 8 consecutive
-// elements of the token's [3, H, Dh] slice, i.e. (s, h, sub) with LPR lanes
-// (Dh = 8 * LPR, LPR divides 32) per (s, h) row.
+// A CTA owns kQkvTok consecutive tokens: thread e8 of the 3*d/8 threads owns
+// 8 consecutive elements of each token's [3, H, Dh] slice, i.e. (s, h, sub)
+// with LPR lanes (Dh = 8 * LPR, LPR divides 32) per (s, h) row.  All global
+// loads (the tokens' qkv rows, rho, and the tokens' rotary rows, staged in
+// shared memory) are issued before any is used.  In place is safe: each
+// thread writes only the elements it read, after reading them.
+constexpr int kQkvTok = 4;
+constexpr int kQkvMaxHalf = 128;   // rotary pairs staged per token (head_dim <= 256)
+
 template <typename T, int LPR>
 __global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
-  const int64_t n = blockIdx.x;                   // token = b * T + t
+  __shared__ __align__(16) float s_cos[kQkvTok][kQkvMaxHalf];
+  __shared__ __align__(16) float s_sin[kQkvTok][kQkvMaxHalf];
+  const int ntok = a.B * a.T;
+  const int n0 = blockIdx.x * kQkvTok;
   const int e8 = threadIdx.x;                     // < 3 * H * LPR
   const int row = e8 / LPR;                       // s * H + h
   const int sub = e8 - row * LPR;
   const int s = row / a.H;
   const int h = row - s * a.H;
   const int e0 = sub * 8;
-  const T* src = reinterpret_cast<const T*>(a.qkv) + (n * 3 * a.H + row) * (int64_t)a.Dh + e0;
+  const int b0 = n0 / a.T;
+  const int t0 = n0 - b0 * a.T;
 
-  float x[8];
-  load8<T>(src, x);
-  const float rho = a.rho[n];
-  // sum of squares across the LPR lanes of this row (groups are lane-aligned)
-  float ss = 0.f;
+  float x[kQkvTok][8];
+  float rho[kQkvTok];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
-#pragma unroll
-  for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-
-  float outv[8];
-  if (s == 2) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) outv[i] = x[i] / rho;
-  } else {
-    float den = sqrtf(ss);
-    if (a.eps > 0.f) den = fmaxf(den, rho * a.eps);
-    const int t = (int)n - ((int)n / a.T) * a.T;
-    const int p0 = e0 >> 1;  // first pair index of this lane
-    float c[4], sn[4];
-    if ((a.rope_half & 3) == 0 && p0 + 4 <= a.rope_half) {
-      float4 cv = *reinterpret_cast<const float4*>(a.cos_tab + (int64_t)t * a.rope_half + p0);
-      float4 sv = *reinterpret_cast<const float4*>(a.sin_tab + (int64_t)t * a.rope_half + p0);
-      c[0] = cv.x; c[1] = cv.y; c[2] = cv.z; c[3] = cv.w;
-      sn[0] = sv.x; sn[1] = sv.y; sn[2] = sv.z; sn[3] = sv.w;
+  for (int k = 0; k < kQkvTok; ++k) {
+    const int n = n0 + k;
+    if (n < ntok) {
+      load8<T>(reinterpret_cast<const T*>(a.qkv) + ((int64_t)n * 3 * a.H + row) * a.Dh + e0, x[k]);
+      rho[k] = a.rho[n];
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const bool rot = p0 + i < a.rope_half;
-        c[i] = rot ? a.cos_tab[(int64_t)t * a.rope_half + p0 + i] : 1.f;
-        sn[i] = rot ? a.sin_tab[(int64_t)t * a.rope_half + p0 + i] : 0.f;
-      }
+      for (int i = 0; i < 8; ++i) x[k][i] = 0.f;
+      rho[k] = 1.f;
     }
+  }
+  // rotary rows of the CTA's tokens -> shared memory
+  const int half = a.rope_half;
+  for (int i = threadIdx.x; i < kQkvTok * half; i += blockDim.x) {
+    const int k = i / half;
+    const int pi = i - k * half;
+    int t = t0 + k;
+    while (t >= a.T) t -= a.T;  // tokens of the next sequence
+    const bool live = n0 + k < ntok;
+    s_cos[k][pi] = live ? a.cos_tab[(int64_t)t * half + pi] : 1.f;
+    s_sin[k][pi] = live ? a.sin_tab[(int64_t)t * half + pi] : 0.f;
+  }
+  float scl[8];
+  if (s < 2) {
     const float* sc = a.qk_scale + (int64_t)h * a.Dh + e0;
     float4 s0 = *reinterpret_cast<const float4*>(sc);
     float4 s1 = *reinterpret_cast<const float4*>(sc + 4);
-    float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float xe = x[2 * i], xo = x[2 * i + 1];
-      float re, ro;
-      if (p0 + i < a.rope_half) {
-        re = xe * c[i] - xo * sn[i];
-        ro = xe * sn[i] + xo * c[i];
-      } else {
-        re = xe;
-        ro = xo;
-      }
-      outv[2 * i] = (re / den) * (scl[2 * i] * a.qk_mult);
-      outv[2 * i + 1] = (ro / den) * (scl[2 * i + 1] * a.qk_mult);
-    }
+    scl[0] = s0.x * a.qk_mult; scl[1] = s0.y * a.qk_mult; scl[2] = s0.z * a.qk_mult; scl[3] = s0.w * a.qk_mult;
+    scl[4] = s1.x * a.qk_mult; scl[5] = s1.y * a.qk_mult; scl[6] = s1.z * a.qk_mult; scl[7] = s1.w * a.qk_mult;
   }
-  T* dst = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v)) + out_offset(a, n, h) + e0;
-  store8<T>(dst, outv);
+  __syncthreads();
+  T* base = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v));
+  const int p0 = e0 >> 1;  // first rotary pair of this lane
+#pragma unroll
+  for (int k = 0; k < kQkvTok; ++k) {
+    const int n = n0 + k;
+    // sum of squares across the LPR lanes of this row (groups are lane-aligned; all lanes take part)
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[k][i] * x[k][i];
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (n >= ntok) continue;
+    float outv[8];
+    // one reciprocal per row, then multiplies (within 1 ulp of dividing each element)
+    if (s == 2) {
+      const float inv_rho = 1.0f / rho[k];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) outv[i] = x[k][i] * inv_rho;
+    } else {
+      float den = sqrtf(ss);
+      if (a.eps > 0.f) den = fmaxf(den, rho[k] * a.eps);
+      const float inv_den = 1.0f / den;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float xe = x[k][2 * i], xo = x[k][2 * i + 1];
+        float re = xe, ro = xo;
+        if (p0 + i < half) {
+          const float c = s_cos[k][p0 + i], sn = s_sin[k][p0 + i];
+          re = xe * c - xo * sn;
+          ro = xe * sn + xo * c;
+        }
+        outv[2 * i] = (re * inv_den) * scl[2 * i];
+        outv[2 * i + 1] = (ro * inv_den) * scl[2 * i + 1];
+      }
+    }
+    store8<T>(base + out_offset(a, n, s, h) + e0, outv);
+  }
 }
 
 template <typename T>
@@ -158,7 +188,7 @@ __global__ void __launch_bounds__(256) qkv_generic_kernel(QkvArgs a) {
   const int s = (int)(ns % 3);
   const int64_t n = ns / 3;
   const T* src = reinterpret_cast<const T*>(a.qkv) + task * (int64_t)a.Dh;
-  T* dst = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v)) + out_offset(a, n, h);
+  T* dst = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v)) + out_offset(a, n, s, h);
   const float rho = a.rho[n];
   if (s == 2) {
     for (int e = lane; e < a.Dh; e += 32) stf<T>(dst, e, ldf<T>(src, e) / rho);
@@ -203,7 +233,14 @@ extern "C" int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rh
                 H, Dh);
   ENGPT_REQUIRE(rope_half >= 0 && 2 * rope_half <= Dh, ENGPT_ERR_SHAPE, "qkv_postprocess: rope_half=%d Dh=%d",
                 rope_half, Dh);
-  ENGPT_REQUIRE(out_layout == 0 || out_layout == 1, ENGPT_ERR_ARG, "qkv_postprocess: layout %d", out_layout);
+  ENGPT_REQUIRE(out_layout >= ENGPT_QKV_BTHD && out_layout <= ENGPT_QKV_INPLACE, ENGPT_ERR_ARG,
+                "qkv_postprocess: layout %d", out_layout);
+  if (out_layout == ENGPT_QKV_INPLACE) {
+    // q, k, v are written over qkv: their pointers must be null or the qkv buffer itself
+    ENGPT_REQUIRE((!q_out || q_out == qkv) && (!k_out || k_out == qkv) && (!v_out || v_out == qkv),
+                  ENGPT_ERR_ARG, "qkv_postprocess: in-place outputs must be the qkv buffer");
+    q_out = k_out = v_out = const_cast<void*>(qkv);
+  }
   ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "qkv_postprocess: dtype %d", dtype);
   if ((int64_t)B * T == 0) return ENGPT_OK;
   ENGPT_REQUIRE(qkv && rho && qk_scale && q_out && k_out && v_out, ENGPT_ERR_ARG, "qkv_postprocess: null pointer");
@@ -214,14 +251,15 @@ extern "C" int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rh
   cudaStream_t st = as_stream(stream);
   const int esz = dtype == ENGPT_BF16 ? 2 : 4;
   const bool vec_ok = (Dh == 8 || Dh == 16 || Dh == 32 || Dh == 64 || Dh == 128 || Dh == 256) &&
+                      rope_half <= kQkvMaxHalf &&
                       aligned(qkv, 16) && aligned(q_out, 16) && aligned(k_out, 16) && aligned(v_out, 16) &&
                       aligned(qk_scale, 16) && (rope_half == 0 || (aligned(cos_tab, 16) && aligned(sin_tab, 16))) &&
                       ((int64_t)Dh * esz) % 16 == 0;
   const int threads_per_token = 3 * H * (Dh / 8);
   if (vec_ok && threads_per_token <= 768 && threads_per_token % 32 == 0) {
     const int lpr = Dh / 8;
-    const int64_t blocks = (int64_t)B * T;
-    ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "qkv_postprocess: too large");
+    ENGPT_REQUIRE((int64_t)B * T <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "qkv_postprocess: too large");
+    const int64_t blocks = ((int64_t)B * T + kQkvTok - 1) / kQkvTok;
 #define ENGPT_QKV_LAUNCH(L)                                                                                  \
   case L:                                                                                                    \
     if (dtype == ENGPT_BF16)                                                                                 \

@@ -96,7 +96,8 @@ def qkv_postprocess_into(qkv: Tensor, rho: Tensor, cos: Tensor, sin: Tensor, qk_
     _lib.call("engpt_qkv_postprocess", qkv.data_ptr(), _lib.dtype_code(qkv.dtype), rho.data_ptr(),
               cos.data_ptr() if cos.numel() else None, sin.data_ptr() if sin.numel() else None, cos.shape[-1],
               qk_scale.data_ptr(), float(qk_mult), float(norm_eps), bsz, seq_len, n_head, head_dim,
-              q.data_ptr(), k.data_ptr(), v.data_ptr(), 1 if head_major else 0, _lib.stream_handle(qkv.device))
+              q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.QKV_BHTD if head_major else _lib.QKV_BTHD,
+              _lib.stream_handle(qkv.device))
 
 
 def qkv_postprocess_from_carried(qkv: Tensor, rho: Tensor, cos: Tensor, sin: Tensor, qk_scale: Tensor,

@@ -9,7 +9,7 @@ forward (engpt/models.py:263-292) on the GPU:
 
   per block (engpt/models.py:140-182)
     qkv      = Y_bf16 @ W_qkv^T                          cuBLAS (plain GEMM)
-    q, k, v  = fused QKV epilogue -> [B,H,T,Dh]          engpt_qkv_postprocess
+    q, k, v  = fused QKV epilogue, in place over qkv     engpt_qkv_postprocess
     attn     = causal attention  -> [B,T,H,Dh]           engpt_causal_attention (tcgen05)
     branch   = attn @ W_o^T                              cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y/rho engpt_carried_residual_gauge
@@ -29,6 +29,7 @@ workspace that is reused across calls; returned logits and loss are fresh.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Callable, Dict, Optional, Tuple
 
@@ -136,10 +137,10 @@ class _Workspace:
         self.y = e(n, d, dtype=torch.float32)
         self.rho = e(n, dtype=torch.float32)
         self.x = e(n, d)                      # GEMM operand: Y (QKV) or Y/rho (up/gate, head)
+        # raw projection [B, T, 3, H, Dh]; the epilogue turns it into q, k, v in place
         self.qkv = e(n, 3 * d)
-        self.q = e(bsz, H, seq_len, Dh)
-        self.k = e(bsz, H, seq_len, Dh)
-        self.v = e(bsz, H, seq_len, Dh)
+        qkv5 = self.qkv.view(bsz, seq_len, 3, H, Dh)
+        self.q, self.k, self.v = qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2]   # [B, T, H, Dh] views
         self.attn = e(n, d)                   # [B, T, H, Dh]
         self.branch = e(n, d)
         self.ug = e(n, 2 * W)
@@ -147,10 +148,8 @@ class _Workspace:
         self.row_loss = e(n, dtype=torch.float32)
         self.cos = e(seq_len, Dh // 2, dtype=torch.float32)
         self.sin = e(seq_len, Dh // 2, dtype=torch.float32)
-        q4, o4 = self.q, self.attn.view(bsz, seq_len, H, Dh)
-        self.attn_strides = torch.tensor(
-            [q4.stride(0), q4.stride(2), q4.stride(1)] * 3 + [o4.stride(0), o4.stride(1), o4.stride(2)],
-            dtype=torch.int64)
+        self.attn_strides = K.attention_strides(self.q, self.k, self.v, self.attn.view(bsz, seq_len, H, Dh),
+                                                head_major=False)
         # bf16 weight copies (re-cast from the fp32 parameters on every forward)
         if bf16:
             self.w = [dict(qkv=e(3 * d, d), out=e(d, d), ug=e(2 * W, d), down=e(d, W)) for _ in range(cfg.n_layer)]
@@ -310,12 +309,18 @@ class EfficientNGPT(nn.Module):
                     _lib.call("engpt_scale_rows_cast", ws.y.data_ptr(), None, 1.0, n, d, ws.x.data_ptr(),
                               _lib.BF16, st)
             if bf16:
+                # autocast's per-forward bf16 copies of the linear weights, in one batched launch
+                srcs, dsts, counts = [], [], []
                 for i, blk in enumerate(self.blocks):
                     w = ws.w[i]
                     for name, p in (("qkv", blk.qkv.weight), ("out", blk.out_proj.weight),
                                     ("ug", blk.up_gate.weight), ("down", blk.down_proj.weight)):
-                        _lib.call("engpt_scale_rows_cast", p.data_ptr(), None, 1.0, p.shape[0], p.shape[1],
-                                  w[name].data_ptr(), _lib.BF16, st)
+                        srcs.append(p.data_ptr())
+                        dsts.append(w[name].data_ptr())
+                        counts.append(p.numel())
+                nw = len(srcs)
+                _lib.call("engpt_cast_f32_bf16_many", (ctypes.c_void_p * nw)(*srcs), (ctypes.c_void_p * nw)(*dsts),
+                          (ctypes.c_int64 * nw)(*counts), nw, st)
             scale = K.ngpt_attention_scale(Dh)
             sqrt_d = math.sqrt(float(d))
             u_mult = sqrt_d if cfg.scale_mlp_u_by_sqrt_d else 1.0
@@ -330,7 +335,7 @@ class EfficientNGPT(nn.Module):
                 torch.mm(x_in, wq.t(), out=ws.qkv)
                 _lib.call("engpt_qkv_postprocess", ws.qkv.data_ptr(), act, ws.rho.data_ptr(), ws.cos.data_ptr(),
                           ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(), float(blk.qk_mult), float(cfg.norm_eps),
-                          bsz, seq_len, H, Dh, ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(), 1, st)
+                          bsz, seq_len, H, Dh, None, None, None, _lib.QKV_INPLACE, st)
                 if self.attn_timer is not None:
                     self.attn_timer("start")
                 _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),

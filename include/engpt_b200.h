@@ -53,6 +53,13 @@ enum engpt_aux_mode {
   ENGPT_AUX_F32_H = 3    /* fp32 Y_out / rho_out (fp32 mode)                            */
 };
 
+/* Output layout of engpt_qkv_postprocess. */
+enum engpt_qkv_layout {
+  ENGPT_QKV_BTHD = 0,     /* q, k, v as separate [B, T, H, Dh] tensors (the reference's return layout)  */
+  ENGPT_QKV_BHTD = 1,     /* q, k, v as separate [B, H, T, Dh] tensors (head-major)                     */
+  ENGPT_QKV_INPLACE = 2   /* written back over qkv [B, T, 3, H, Dh] (q_out/k_out/v_out: NULL or qkv) */
+};
+
 /* Attention kernel selection (engpt_causal_attention `impl`). */
 enum engpt_attn_impl {
   ENGPT_ATTN_AUTO = 0,   /* tcgen05 kernel when bf16 and head_dim in {64,128}, else SIMT */
@@ -83,8 +90,9 @@ ENGPT_API int engpt_clear_device_status(void);
  * rho: [B, T] fp32.  cos_tab/sin_tab: [T, rope_half] fp32 (rope_half = Dh/2
  * rounded down, as rotary_frequencies builds them).  qk_scale: [H, Dh] fp32;
  * the scale applied is qk_scale * qk_mult (pass 1.0 for an effective scale).
- * Outputs q, k, v in `dtype`, laid out [B, T, H, Dh] (out_layout 0, the
- * reference's) or [B, H, T, Dh] (out_layout 1, head-major for attention).
+ * Outputs q, k, v in `dtype`, laid out as engpt_qkv_layout says: separate
+ * [B, T, H, Dh] or [B, H, T, Dh] tensors, or in place over qkv (the layout
+ * the reference's no-grad path leaves, engpt/kernels.py:174-178).
  */
 ENGPT_API int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rho,
                           const float* cos_tab, const float* sin_tab, int rope_half,
@@ -149,6 +157,15 @@ ENGPT_API int engpt_swiglu(const void* ug, int dtype, const float* s_u, const fl
  */
 ENGPT_API int engpt_scale_rows_cast(const float* src, const float* scale, float mult, int64_t rows,
                           int64_t cols, void* out, int out_dtype, void* stream);
+
+/*
+ * Batched fp32 -> bf16 cast of n tensors (src[i], dst[i], counts[i] elements)
+ * in one launch per 64 tensors: the bf16 copies of the linear weights that
+ * autocast makes on every forward (engpt/models.py:142,152,166,172 under
+ * torch.autocast).  src/dst/counts are host arrays of device pointers.
+ */
+ENGPT_API int engpt_cast_f32_bf16_many(const void* const* src, void* const* dst, const int64_t* counts, int n,
+                                       void* stream);
 
 /*
  * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).

@@ -72,6 +72,29 @@ def test_qkv_postprocess_layouts_vs_oracle(cuda, dh, dtype):
                                    rtol=tol)
 
 
+@pytest.mark.parametrize("dh,H", [(64, 16), (128, 4), (16, 2)])
+def test_qkv_postprocess_in_place_vs_oracle(cuda, dh, H):
+    """q, k, v written back over the [B, T, 3, H, Dh] projection (the engine's layout)."""
+    rng = np.random.default_rng(dh + H)
+    B, T = 2, 45
+    qkv = rng.standard_normal((B, T, 3, H, dh)) * 2.0
+    rho = rng.uniform(0.5, 600.0, (B, T))
+    cos, sin = O.rotary_frequencies(T, dh, 10000.0)
+    scale = rng.uniform(0.9, 1.1, (H, dh))
+    buf = t(qkv, cuda, torch.bfloat16)
+    ref = O.qkv_postprocess_from_carried(buf.float().cpu().numpy().astype(np.float64),
+                                         rho.astype(np.float32).astype(np.float64), cos.astype(np.float64),
+                                         sin.astype(np.float64), scale.astype(np.float32).astype(np.float64), 1e-6)
+    rho_d, cos_d, sin_d, sc_d = t(rho, cuda), t(cos, cuda), t(sin, cuda), t(scale, cuda)
+    _lib.call("engpt_qkv_postprocess", buf.data_ptr(), _lib.BF16, rho_d.data_ptr(), cos_d.data_ptr(),
+              sin_d.data_ptr(), dh // 2, sc_d.data_ptr(), 1.0, 1e-6, B, T, H, dh, None, None, None,
+              _lib.QKV_INPLACE, _lib.stream_handle(cuda))
+    got = buf.float().cpu().numpy()
+    for s_idx in range(3):
+        exp = ref[s_idx]
+        np.testing.assert_allclose(got[:, :, s_idx], exp, atol=1e-2 * np.abs(exp).max(), rtol=1e-2)
+
+
 @pytest.mark.parametrize("tag,max_radius", [("g075", 0.75), ("g1024", 1024.0), ("g0", 0.0)])
 def test_carried_residual_gauge_fp32_matches_reference(golden, cuda, tag, max_radius):
     g = golden("ops_small.npz")
@@ -238,6 +261,20 @@ def test_swiglu_vs_oracle(cuda, dtype):
     exp = u * O.silu(gg)
     tol = 1e-5 if dtype == torch.float32 else 8e-3
     np.testing.assert_allclose(out.float().cpu().numpy(), exp, rtol=tol, atol=tol * np.abs(exp).max())
+
+
+def test_cast_f32_bf16_many_matches_torch(cuda):
+    import ctypes
+    g = torch.Generator().manual_seed(3)
+    srcs = [torch.randn(n, generator=g).to(cuda) for n in (1, 7, 8, 1000, 4096 * 3 + 5)]
+    srcs.append(torch.randn(64, 70, generator=g).to(cuda)[:, 3:67].contiguous())
+    dsts = [torch.empty(x.shape, device=cuda, dtype=torch.bfloat16) for x in srcs]
+    n = len(srcs)
+    _lib.call("engpt_cast_f32_bf16_many", (ctypes.c_void_p * n)(*[x.data_ptr() for x in srcs]),
+              (ctypes.c_void_p * n)(*[x.data_ptr() for x in dsts]),
+              (ctypes.c_int64 * n)(*[x.numel() for x in srcs]), n, _lib.stream_handle(cuda))
+    for x, y in zip(srcs, dsts):
+        assert torch.equal(y, x.to(torch.bfloat16))
 
 
 @pytest.mark.parametrize("V", [1001, 50257])
