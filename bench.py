@@ -91,7 +91,7 @@ def load_peaks():
 
 def load_traffic():
     """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "attention_tcgen05_L16_d1024_T2048.md")
+    path = os.path.join(ROOT, "profiles", "attn_fwd2_B32_H16_T2048_D64.md")
     if not os.path.exists(path):
         return None
     for line in open(path):
@@ -220,7 +220,7 @@ LAUNCHES = {"engpt_cross_entropy": 2}
 def run_gpu(a, world, rank, local_rank):
     import torch
     import torch.distributed as dist
-    from engpt_b200 import EfficientNGPT, _lib
+    from engpt_b200 import EfficientNGPT, _lib, sharding
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -243,12 +243,13 @@ def run_gpu(a, world, rank, local_rank):
 
     _lib.call = counting_call
 
+    n_valid = sharding.valid_targets(tgt_d)  # this shard's counted targets (device scalar)
+
     def step(idx, tgt):
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             logits, loss = model(idx, tgt)
-        if world > 1:
-            dist.all_reduce(loss, op=dist.ReduceOp.SUM)
-            loss = loss / world
+        if world > 1:  # token-weighted mean over all shards: one NCCL all-reduce of 2 doubles
+            loss = sharding.combine_loss(loss, n_valid)
         return logits, loss
 
     for _ in range(max(a.warmup, 1)):
@@ -331,7 +332,7 @@ def run_gpu(a, world, rank, local_rank):
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * idx_h.numel() * idx_h.element_size() * world,
                 "d2h_bytes_per_step": 4 * world},
         "gpu_launches": launches,
-        "roofline": {"kernel": "attn_fwd_kernel<64> (tcgen05)", "bound": "tensor", "achieved": achieved,
+        "roofline": {"kernel": "attn_fwd2_kernel (tcgen05, head_dim 64)", "bound": "tensor", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(),
                      "peak_source": f"{peaks['source']} bf16 sustained",
                      "avg_launch_ms": attn_avg, "flops_per_launch": attn_flops},
@@ -457,7 +458,7 @@ def run_attention(a, world, rank, local_rank):
         "dtype": "bf16", "data": "synthetic (seeded normal q/k/v, unit q/k scaled by U(0.9,1.1))",
         "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh)",
                    "l2": "inputs read once per launch; no flush between launches"},
-        "roofline": {"kernel": f"attn_fwd_kernel<{Dh}> (tcgen05)", "bound": "tensor", "achieved": achieved,
+        "roofline": {"kernel": "attn_fwd2_kernel (tcgen05)" if Dh == 64 else f"attn_fwd_kernel<{Dh}> (tcgen05)", "bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                      "traffic": None, "peak_source": f"{peaks['source']} bf16 burst"},
         "torch_sdpa_bf16": {"ms": ms_torch, "tflops": flops / (ms_torch / 1000.0) / 1e12},

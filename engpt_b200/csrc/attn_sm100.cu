@@ -1,22 +1,14 @@
 // Causal flash attention for B200 (sm_100a): tcgen05 MMA with TMEM
-// accumulators, TMA-staged Q/K/V tiles, online softmax in registers.
+// accumulators, TMA-staged Q/K/V tiles, online softmax from TMEM.
 //
 // Computes causal_sdpa (engpt/kernels.py:417-431) with the nGPT scale
 // sqrt(Dh) (engpt/kernels.py:434-435) for bf16 inputs and head_dim 64 / 128.
 //
-// One CTA owns a 128-query tile of one (batch, head) and walks the causal
-// prefix of 128-key tiles.  Warp roles (192 threads):
-//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
-//   warp 1      TMEM allocator + MMA issuer (one thread):
-//                 S_j = Q K_j^T       -> TMEM S[j % 2]   (fp32, 128 columns)
-//                 O  += P_{j-1} V_{j-1} -> TMEM O        (fp32, Dh columns)
-//   warps 2..5  softmax: thread i owns query row i (TMEM lane i); reads S_j
-//               with tcgen05.ld, applies the causal mask, exponentiates in
-//               base 2 against a per-row reference max and writes P_j (bf16)
-//               into a 128B-swizzled shared tile, the A operand of the PV MMA.
-// The per-row reference max is only raised (rescaling O in TMEM) when the
-// tile max exceeds it by more than 2^8, so the usual case does no O round
-// trip; exponentials stay <= 256 and the final O / l is exact.
+// Two kernels:
+//   attn_fwd_kernel<D>  (namespace attn_tc): one 128-query tile per CTA, P
+//     staged in shared memory; serves head_dim 128 (and head_dim 64 on request).
+//   attn_fwd2_kernel    (namespace attn_tc::v2): head_dim 64, two 128-query
+//     tiles per CTA, S / P / O all in TMEM, 16 softmax warps (see below).
 // Every wait is bounded (see mbar_wait); on a timeout the kernel records
 // ENGPT_ERR_TIMEOUT in the device status word, drains its own copies and
 // MMAs, frees TMEM and returns.
@@ -74,6 +66,19 @@ struct Params {
   float scale_log2;
 };
 
+// One CTA owns a 128-query tile of one (batch, head) and walks the causal
+// prefix of 128-key tiles.  Warp roles (192 threads):
+//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1      TMEM allocator + MMA issuer (one thread):
+//                 S_j = Q K_j^T       -> TMEM S[j % 2]   (fp32, 128 columns)
+//                 O  += P_{j-1} V_{j-1} -> TMEM O        (fp32, Dh columns)
+//   warps 2..5  softmax: thread i owns query row i (TMEM lane i); reads S_j
+//               with tcgen05.ld, applies the causal mask, exponentiates in
+//               base 2 against a per-row reference max and writes P_j (bf16)
+//               into a 128B-swizzled shared tile, the A operand of the PV MMA.
+// The per-row reference max is only raised (rescaling O in TMEM) when the
+// tile max exceeds it by more than 2^8, so the usual case does no O round
+// trip; exponentials stay <= 256 and the final O / l is exact.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -331,22 +336,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ============================================================================
 // Head dim 64: two 128-query tiles per CTA (a 256-query band of one (b, h))
-// share every K/V tile.  Two softmax warpgroups (A: rows 0..127, B: rows
-// 128..255) ping-pong against one MMA-issuing thread; S, P and O all live in
-// TMEM (512 columns: S_A | S_B | P_A | P_B | O_A | O_B), P is written with
-// tcgen05.st as packed bf16 and consumed by the PV MMA straight from TMEM, so
-// the softmax never touches shared memory.  The exponentials are split
-// between the MUFU unit (ex2.approx) and an FMA-pipe polynomial (exp2_poly2)
-// on off-diagonal tiles; scale/subtract, row sums and the polynomial use the
-// packed f32x2 FMA/ADD.
+// share every K/V tile.  Jobs run in the order (A,0) (B,0) (A,1) (B,1) ...
+// (tile B owns one more, its diagonal, tile).  TMEM (512 columns) holds three
+// 128-column score slots that the jobs rotate through (job g uses slot g % 3)
+// and the two O accumulators (64 columns each).  The softmax turns a slot's
+// fp32 scores S into bf16 P in place and the PV MMA reads P from TMEM, so the
+// softmax never touches shared memory.  With three slots the MMA warp computes
+// the next S of a tile while that tile's softmax is still exponentiating the
+// current one; a slot is refilled only after the PV that read its P completed
+// (waited on its own mbarrier: tcgen05 orders MMAs only within one accumulator).
+//
+// Softmax: 16 warps, 4 per SM sub-partition.  A tile's 128 rows are shared by
+// 8 warps: warp (tile, half, quarter) owns TMEM lanes 32*quarter.. and the
+// score columns 64*half .. 64*half+63 of those rows.  Exponentials are base 2
+// against a per-row reference max m that only rises: a 32-score chunk is
+// exponentiated, and if its sum exceeds 2^8 (so some x > 3) the half raises
+// its m to ceil(chunk max) - 2, scaling its stored P of the tile and its l by
+// the exact power of two 2^-k, and redoes the chunk.  At the end of a tile
+// the two halves of a row agree on the larger raise (a bounded mbarrier
+// handshake), the half that raised less rescales its P, and O is rescaled
+// (each half its 32 columns) after the previous PV completed.  Every stored
+// value stays <= 2^8 and the final O / l is exact.  Fully masked chunks of a
+// diagonal tile are written as zeros without exponentiating.
 // ============================================================================
 namespace v2 {
 
 constexpr int D = 64;
 constexpr int BN = 128;              // keys per KV tile
 constexpr int NS = 3;                // K/V pipeline stages
-constexpr int kThreads = 384;        // warps 0: TMA, 1: MMA, 2-3: idle, 4-7: softmax A, 8-11: softmax B
-constexpr int kPolyPer16 = 6;        // of every 16 scores on an off-diagonal tile, this many use the polynomial
+constexpr int NSLOT = 3;             // TMEM score slots
+constexpr int kSoftmaxWarps = 16;
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;   // warps 0-15 softmax, 16 TMA, 17 MMA
+constexpr int kWarpTMA = 16;
+constexpr int kWarpMMA = 17;
 
 struct Layout {
   static constexpr int QA = 0;
@@ -354,122 +376,165 @@ struct Layout {
   static constexpr int K = QB + kBlockBytes;             // NS stages x 16 KB
   static constexpr int V = K + NS * kBlockBytes;         // NS stages x 16 KB
   static constexpr int BAR = V + NS * kBlockBytes;
-  static constexpr int kBars = 24;
-  static constexpr int MISC = BAR + kBars * 8;
+  static constexpr int kBars = 32;
+  static constexpr int XCH = BAR + kBars * 8;            // float [2 parity][2 tile][2 half][128 rows]
+  static constexpr int MISC = XCH + 2 * 2 * 2 * 128 * 4;
   static constexpr int TOTAL = MISC + 16;
   static constexpr int kDynSmem = TOTAL + 1024;
 };
 
 enum {
   B_Q = 0,
-  B_KFULL = 1,                 // + stage (NS)
-  B_VFULL = B_KFULL + NS,      // + stage
-  B_KVEMPTY = B_VFULL + NS,    // + stage
-  B_SFULL = B_KVEMPTY + NS,    // + warpgroup (2): S_w(j) written
-  B_TDONE = B_SFULL + 2,       // + warpgroup: S_w(j) consumed and P_w(j) written (128 arrivals)
-  B_PVDONE = B_TDONE + 2,      // + warpgroup: PV_w(j) complete
-  B_FINAL = B_PVDONE + 2
+  B_KFULL = 1,                   // + stage (NS)
+  B_VFULL = B_KFULL + NS,        // + stage
+  B_KVEMPTY = B_VFULL + NS,      // + stage
+  B_SFULL = B_KVEMPTY + NS,      // + slot: S of the slot's current job written
+  B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
+  B_PVDONE = B_TDONE + NSLOT,    // + slot: the PV that read the slot's P completed
+  B_ODONE = B_PVDONE + NSLOT,    // + 2 * tile + (j & 1): PV(tile, j) and every MMA before it completed
+  B_FINAL = B_ODONE + 4,
+  B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
-static_assert(B_FINAL < Layout::kBars, "barrier slots");
+static_assert(B_PAIR + 8 <= Layout::kBars, "barrier slots");
 
-// TMEM columns
-constexpr uint32_t kColS = 0;     // + 128 * w
-constexpr uint32_t kColP = 256;   // + 64 * w   (bf16 pairs: 128 keys in 64 columns)
-constexpr uint32_t kColO = 384;   // + 64 * w
+constexpr uint32_t kColO = 384;      // + 64 * tile; slots at 128 * slot
 
-// One 32-score chunk of a row: x = score * scale*log2(e) - m, exponentiate,
-// pack to 16 bf16 pairs, add the pair sums to l2 and track max(x).
-// MIXED sends kPolyPer16 of every 16 scores to the FMA polynomial (only used
-// on tiles without masked scores); otherwise all go to MUFU.
-template <bool MIXED>
-__device__ __forceinline__ void exp_chunk(const uint32_t* r, uint64_t sc2, uint64_t nm2, uint64_t& l2, float& mx,
-                                          uint32_t* pw) {
+// Job list of one band: tile A (rows q0..q0+127) has nA KV tiles, tile B (rows q0+128..) nB = nA + 1
+// when it has rows inside the sequence, else 0.
+struct Band {
+  int nA, nB;
+  __device__ __forceinline__ int jobs() const { return nA + nB; }
+  __device__ __forceinline__ void job(int g, int& w, int& j) const {
+    if (nB == 0) {
+      w = 0;
+      j = g;
+    } else if (g < 2 * nA) {
+      w = g & 1;
+      j = g >> 1;
+    } else {
+      w = 1;
+      j = nA;
+    }
+  }
+  __device__ __forceinline__ int job_of(int w, int j) const { return nB == 0 ? j : (j < nA ? 2 * j + w : 2 * nA); }
+};
+
+// TMEM column of the bf16 P pair for keys 2i, 2i+1 of a slot, i < 64: each half writes its 32 P columns
+// over the first half of its own score columns (half 0: 0..31, half 1: 64..95).
+__host__ __device__ constexpr uint32_t p_col(int i) { return i < 32 ? (uint32_t)i : (uint32_t)(i + 32); }
+
+// Exponentiate 16 pairs x -> bf16 pairs pw on MUFU ex2 (ex2(-inf) = 0 for masked scores), returning the
+// pair sums of the fp32 exponentials.
+__device__ __forceinline__ uint64_t exp_pairs(const uint64_t* xs, uint32_t* pw) {
+  uint64_t ca = f2_pack(0.f, 0.f), cb = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const uint64_t x = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
     float x0, x1;
-    f2_unpack(x, x0, x1);
-    mx = fmaxf(mx, fmaxf(x0, x1));
-    uint64_t e;
-    if (MIXED && ((2 * i) & 15) < kPolyPer16) {
-      e = exp2_poly2(f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f)));
-    } else {
-      e = f2_pack(ex2_approx(x0), ex2_approx(x1));
-    }
-    l2 = fadd2(l2, e);
-    float e0, e1;
-    f2_unpack(e, e0, e1);
+    f2_unpack(xs[i], x0, x1);
+    const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
+    if (i & 1)
+      cb = fadd2(cb, f2_pack(e0, e1));
+    else
+      ca = fadd2(ca, f2_pack(e0, e1));
     pw[i] = pack_bf16x2(e0, e1);
   }
+  return fadd2(ca, cb);
 }
 
-// Exponentiate the row's scores of one tile from TMEM S into TMEM P, chunk by chunk.
-__device__ __forceinline__ void exp_tile(uint32_t tS, uint32_t tP, bool diag, int kbase, int q_idx, float sl2,
-                                         float m, uint64_t& l2, float& mx) {
-  const uint64_t sc2 = f2_pack(sl2, sl2);
-  const uint64_t nm2 = f2_pack(-m, -m);
-  const bool any_diag = __any_sync(0xffffffffu, diag);
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    uint32_t pw[16];
-    tmem_ld32(tS + c, r);
-    tmem_wait_ld();
-    if (any_diag) {
+// x = score * scale*log2(e) - m for 32 raw fp32 scores; -inf where the key comes after the query.
+__device__ __forceinline__ void scaled_scores(const uint32_t* r, uint64_t sc2, uint64_t nm2, bool mask, int key0,
+                                              int q_idx, uint64_t* xs) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (kbase + c + i > q_idx) r[i] = __float_as_uint(-INFINITY);
-      exp_chunk<false>(r, sc2, nm2, l2, mx, pw);
-    } else {
-      exp_chunk<true>(r, sc2, nm2, l2, mx, pw);
+  for (int i = 0; i < 16; ++i) xs[i] = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
+  if (mask) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float x0, x1;
+      f2_unpack(xs[i], x0, x1);
+      if (key0 + 2 * i > q_idx) x0 = -INFINITY;
+      if (key0 + 2 * i + 1 > q_idx) x1 = -INFINITY;
+      xs[i] = f2_pack(x0, x1);
     }
-    tmem_st16(tP + c / 2, pw);
   }
 }
 
-// Row max of the raw scores of one tile (masked), read from TMEM S.
-__device__ __forceinline__ float max_tile(uint32_t tS, int kbase, int q_idx) {
-  float mx = -INFINITY;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    tmem_ld32(tS + c, r);
-    tmem_wait_ld();
+// Multiply 16 TMEM columns of this row by f: fp32 values (O) or bf16 pairs (P, f a power of two: exact).
+template <bool BF16>
+__device__ __forceinline__ void scale_cols16(uint32_t taddr, float f) {
+  uint32_t w[16];
+  tmem_ld16(taddr, w);
+  tmem_wait_ld16(w);
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (kbase + c + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
-  }
-  return mx;
-}
-
-// Multiply the D fp32 columns of O (this row) by f.
-__device__ __forceinline__ void scale_o(uint32_t tO, float f) {
-#pragma unroll
-  for (int c = 0; c < D; c += 32) {
-    uint32_t o[32];
-    tmem_ld32(tO + c, o);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-    tmem_st32(tO + c, o);
-  }
-}
-
-// Multiply the 128 bf16 P values of this row (64 columns) by f (a power of two: exact).
-__device__ __forceinline__ void scale_p(uint32_t tP, float f) {
-#pragma unroll
-  for (int c = 0; c < 64; c += 32) {
-    uint32_t w[32];
-    tmem_ld32(tP + c, w);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < 16; ++i) {
+    if (BF16) {
       __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&w[i]);
       float2 fv = __bfloat1622float2(v);
       w[i] = pack_bf16x2(fv.x * f, fv.y * f);
+    } else {
+      w[i] = __float_as_uint(__uint_as_float(w[i]) * f);
     }
-    tmem_st32(tP + c, w);
   }
+  tmem_st16(taddr, w);
+}
+
+__device__ __forceinline__ float pow2_neg(float k) {   // exactly 2^-k for an integer k >= 0 (0 below 2^-125)
+  return (k >= 126.0f) ? 0.0f : __int_as_float((127 - (int)k) << 23);
+}
+
+// Per-row softmax state of one softmax thread (its half of the row).
+struct RowState {
+  float m;        // reference max at the start of the tile, log2 units (equal in both halves)
+  float kr;       // this half's raise of m during the current tile
+  uint64_t l2;    // this half's running sum of exponentials (two partial sums)
+};
+
+// One 32-score chunk (raw fp32 scores in r, keys key0..key0+31) -> 16 bf16 pairs at TMEM column tP.
+// tP0 / n_prev: the P columns this half already wrote in this tile (rescaled on a raise).
+__device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, uint32_t tP0, int n_prev, int key0,
+                                              int q_idx, float sl2, bool diag, RowState& st) {
+  uint32_t pw[16];
+  bool mask = false;
+  if (diag) {
+    if (__all_sync(0xffffffffu, key0 > q_idx)) {   // every key after every query of the warp: P = 0
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pw[i] = 0u;
+      tmem_st16(tP, pw);
+      return;
+    }
+    mask = __any_sync(0xffffffffu, key0 + 31 > q_idx);
+  }
+  const float m = st.m + st.kr;
+  uint64_t xs[16];
+  scaled_scores(r, f2_pack(sl2, sl2), f2_pack(-m, -m), mask, key0, q_idx, xs);
+  uint64_t c2 = exp_pairs(xs, pw);
+  float s0, s1;
+  f2_unpack(c2, s0, s1);
+  if (__any_sync(0xffffffffu, s0 + s1 > 256.0f)) {
+    // rare: a value above 2^3.  Raise this half's m to ceil(chunk max) - 2 and redo the chunk.
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float x0, x1;
+      f2_unpack(xs[i], x0, x1);
+      mx = fmaxf(mx, fmaxf(x0, x1));
+    }
+    const float k = (s0 + s1 > 256.0f) ? ceilf(mx) - 2.0f : 0.0f;   // >= 2 when raised
+    const float f = pow2_neg(k);
+    st.kr += k;
+    float la, lb;
+    f2_unpack(st.l2, la, lb);
+    st.l2 = f2_pack(la * f, lb * f);
+    if (n_prev > 0) {
+      tmem_wait_st();
+      scale_cols16<true>(tP0, f);
+    }
+    const uint64_t k2 = f2_pack(k, k);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) xs[i] = fsub2(xs[i], k2);
+    c2 = exp_pairs(xs, pw);
+  }
+  st.l2 = fadd2(st.l2, c2);
+  tmem_st16(tP, pw);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -494,10 +559,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bh / p.H;
   const int h = bh % p.H;
   const int q0 = band * 256;
-  const bool b_live = q0 + 128 < p.T;          // tile B has rows inside the sequence
-  const int nA = 2 * band + 1;                 // KV tiles 0..2*band (diagonal at 2*band)
-  const int nB = b_live ? 2 * band + 2 : 0;    // KV tiles 0..2*band+1 (diagonal at 2*band+1)
-  const int n_kv = b_live ? nB : nA;
+  Band bd;
+  bd.nA = 2 * band + 1;                          // KV tiles 0..2*band (diagonal at 2*band)
+  bd.nB = (q0 + 128 < p.T) ? 2 * band + 2 : 0;   // KV tiles 0..2*band+1 (diagonal at 2*band+1)
+  const int n_kv = bd.nB ? bd.nB : bd.nA;
+  const int n_jobs = bd.jobs();
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
@@ -506,16 +572,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_VFULL + s), 1);
       mbar_init(bar(B_KVEMPTY + s), 1);
     }
-    for (int w = 0; w < 2; ++w) {
-      mbar_init(bar(B_SFULL + w), 1);
-      mbar_init(bar(B_TDONE + w), 128);
-      mbar_init(bar(B_PVDONE + w), 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(bar(B_SFULL + s), 1);
+      mbar_init(bar(B_TDONE + s), 256);
+      mbar_init(bar(B_PVDONE + s), 1);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(bar(B_ODONE + i), 1);
     mbar_init(bar(B_FINAL), 1);
+    for (int i = 0; i < 8; ++i) mbar_init(bar(B_PAIR + i), 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == kWarpMMA) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
     tc_fence_before();
@@ -524,15 +592,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kWarpTMA) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(bar(B_Q), (b_live ? 2 : 1) * 128 * D * 2);
+      mbar_expect_tx(bar(B_Q), (bd.nB ? 2 : 1) * 128 * D * 2);
       tma_load_4d(sbase + L::QA, &tmQ, 0, q0, h, b, bar(B_Q));
-      if (b_live) tma_load_4d(sbase + L::QB, &tmQ, 0, q0 + 128, h, b, bar(B_Q));
+      if (bd.nB) tma_load_4d(sbase + L::QB, &tmQ, 0, q0 + 128, h, b, bar(B_Q));
       int last_use[NS];
       for (int s = 0; s < NS; ++s) last_use[s] = -1;
       bool ok = true;
@@ -549,6 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         last_use[s] = j / NS;
       }
       if (!ok || *abort_flag) {
+        // drain the copies still in flight before the CTA exits
         volatile int never = 0;
         mbar_wait(bar(B_Q), 0, &never, 0);
         for (int s = 0; s < NS; ++s) {
@@ -559,144 +628,180 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMMA) {
     // ------------------------------------------------------------ MMA issuer
-    // iteration j: for each tile w, once its softmax finished tile j-1:
-    //   S_w(j) = Q_w K_j^T  (so the softmax can start tile j)  then  O_w += P_w(j-1) V_{j-1}
-    if (lane == 0) {
-      constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
-      constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
-      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, 22);
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        const int s = j % NS;
-        const int s2 = (j + NS - 1) % NS;
-        if (j < n_kv) {
-          ok = mbar_wait(bar(B_KFULL + s), (j / NS) & 1, abort_flag, 23);
-          if (!ok) break;
-        }
-        if (j >= 1) {
-          ok = mbar_wait(bar(B_VFULL + s2), ((j - 1) / NS) & 1, abort_flag, 25);
-          if (!ok) break;
-        }
-        for (int w = 0; w < 2; ++w) {
-          const int nw = (w == 0) ? nA : nB;
-          if (j >= 1 && j - 1 < nw) {
-            ok = mbar_wait(bar(B_TDONE + w), (j - 1) & 1, abort_flag, 24);
-            if (!ok) break;
-          }
-          tc_fence_after();
-          if (j < nw) {
-            const uint32_t qbase = sbase + (w == 0 ? L::QA : L::QB);
+    // S(0), S(1), S(2); then for each job g: PV(g) once its P is written, and S(g+3) into the same slot
+    // once that PV completed.  The whole warp runs the loop (operands stay warp-uniform); one elected lane
+    // issues each MMA and commit.
+    constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
+    constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
+    const uint64_t dqa = sw128_desc(sbase + L::QA, 16, 1024);
+    const uint64_t dqb = sw128_desc(sbase + L::QB, 16, 1024);
+    const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
+    const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
+    auto wait_all = [&](int i, uint32_t parity, int site) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(i), parity, abort_flag, site));
+    };
+    auto issue_s = [&](int g) -> bool {
+      int w, j;
+      bd.job(g, w, j);
+      const int s = j % NS;
+      if (!wait_all(B_KFULL + s, (j / NS) & 1, 23)) return false;
+      tc_fence_after();
+      const uint64_t da = w ? dqb : dqa;
+      const uint64_t db = desc_add(dk0, s * kBlockBytes);
+      const uint32_t td = tmem + 128 * (g % NSLOT);
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t qa = qbase + kk * 32;
-              const uint32_t ka = sbase + L::K + s * kBlockBytes + kk * 32;
-              umma_f16_ss(tmem + kColS + 128 * w, sw128_desc(qa, 16, 1024), sw128_desc(ka, 16, 1024), kIdescS,
-                          kk > 0);
-            }
-            umma_commit(bar(B_SFULL + w));
-          }
-          if (j >= 1 && j - 1 < nw) {
+      for (int kk = 0; kk < D / 16; ++kk)
+        umma_f16_ss_w(td, desc_add(da, kk * 32), desc_add(db, kk * 32), kIdescS, kk > 0 ? 1u : 0u);
+      umma_commit_w(bar(B_SFULL + g % NSLOT));
+      return true;
+    };
+    bool ok = wait_all(B_Q, 0, 22);
+    for (int g = 0; ok && g < NSLOT && g < n_jobs; ++g) ok = issue_s(g);
+    for (int g = 0; ok && g < n_jobs; ++g) {
+      int w, j;
+      bd.job(g, w, j);
+      const int slot = g % NSLOT;
+      const int s = j % NS;
+      ok = wait_all(B_TDONE + slot, (g / NSLOT) & 1, 24);
+      if (!ok) break;
+      ok = wait_all(B_VFULL + s, (j / NS) & 1, 25);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t db = desc_add(dv0, s * kBlockBytes);
+      const uint32_t ta = tmem + 128 * slot;
+      const uint32_t td = tmem + kColO + 64 * w;
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint32_t va = sbase + L::V + s2 * kBlockBytes + kk * 16 * 128;
-              umma_f16_ts(tmem + kColO + 64 * w, tmem + kColP + 64 * w + kk * 8, sw128_desc(va, kBlockBytes, 1024),
-                          kIdescPV, (j - 1 > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(bar(B_PVDONE + w));
-          }
-        }
+      for (int kk = 0; kk < BN / 16; ++kk)   // keys 16kk.. : P columns p_col(8kk)..
+        umma_f16_ts_w(td, ta + p_col(8 * kk), desc_add(db, kk * 16 * 128), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+      umma_commit_w(bar(B_PVDONE + slot));
+      umma_commit_w(bar(B_ODONE + 2 * w + (j & 1)));
+      if (bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
+      if (g + NSLOT < n_jobs) {
+        ok = wait_all(B_PVDONE + slot, (g / NSLOT) & 1, 26);
         if (!ok) break;
-        if (j >= 1) umma_commit(bar(B_KVEMPTY + s2));
+        ok = issue_s(g + NSLOT);
       }
-      umma_commit(bar(B_FINAL));
-      volatile int never = 0;
-      mbar_wait(bar(B_FINAL), 0, &never, 27);
     }
-  } else if (warp >= 4) {
+    umma_commit_w(bar(B_FINAL));
+    volatile int never = 0;
+    mbar_wait(bar(B_FINAL), 0, &never, 27);
+  } else {
     // ------------------------------------------------------------ softmax
-    const int w = (warp - 4) >> 2;             // 0: tile A, 1: tile B
+    const int w = warp >> 3;                   // 0: tile A, 1: tile B
+    const int hf = (warp >> 2) & 1;            // score columns 64*hf .. 64*hf+63
     const int wq = warp & 3;                   // TMEM lane quarter
     const int row = wq * 32 + lane;
     const int q_idx = q0 + 128 * w + row;
     const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + kColS + 128 * w + t_lane;
-    const uint32_t tP = tmem + kColP + 64 * w + t_lane;
-    const uint32_t tO = tmem + kColO + 64 * w + t_lane;
-    const int n_w = (w == 0) ? nA : nB;
+    const uint32_t tO = tmem + kColO + 64 * w + 32 * hf + t_lane;   // this half's 32 O columns
+    const int n_w = (w == 0) ? bd.nA : bd.nB;
     const float sl2 = p.scale_log2;
-    float m_used = 0.f;                        // reference max (log2 units) of this row
-    uint64_t l2 = f2_pack(0.f, 0.f);
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);
+    auto xslot = [&](int par, int half) -> float* { return xch + ((par * 2 + w) * 2 + half) * 128 + row; };
+    const uint32_t pair = bar(B_PAIR + 4 * w + wq);
+    uint32_t pair_phase = 0;
+    // the two halves of these rows swap one value through shared memory (bounded mbarrier handshake)
+    auto swap = [&](float mine, int par, bool& good) -> float {
+      *xslot(par, hf) = mine;
+      mbar_arrive(pair);
+      good = good && __all_sync(0xffffffffu, mbar_wait(pair, pair_phase & 1, abort_flag, 33));
+      ++pair_phase;
+      return *xslot(par, hf ^ 1);
+    };
+    RowState st;
+    st.m = 0.f;
+    st.kr = 0.f;
+    st.l2 = f2_pack(0.f, 0.f);
     bool ok = true;
     for (int j = 0; j < n_w; ++j) {
-      ok = mbar_wait(bar(B_SFULL + w), j & 1, abort_flag, 28);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      const int g = bd.job_of(w, j);
+      const int slot = g % NSLOT;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (g / NSLOT) & 1, abort_flag, 28));
+      if (!ok) break;
+      // O completion barriers alternate by tile parity, and each tile first waits for the PV two tiles
+      // back, so any later parity wait on them is never more than one phase behind
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + 2 * w + (j & 1)), ((j - 2) >> 1) & 1, abort_flag, 29));
+        if (!ok) break;
+      }
       tc_fence_after();
-      const int kbase = j * BN;
-      const bool diag = kbase + BN - 1 > q_idx;
-      if (j == 0) m_used = max_tile(tS, kbase, q_idx) * sl2;
-      if (j >= 1) {
-        // P columns were read by PV_w(j-1), and O must be complete before any rescale
-        ok = mbar_wait(bar(B_PVDONE + w), (j - 1) & 1, abort_flag, 30);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc_fence_after();
+      const uint32_t tS = tmem + 128 * slot + t_lane;
+      const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
+      const int kbase = j * BN + 64 * hf;    // this half's first key
+      const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
+      uint32_t r[32];
+      if (j == 0) {
+        // common reference max: the larger of the two halves' first-chunk maxima (key 0 is always visible)
+        tmem_ld32(tS + 64 * hf, r);
+        tmem_wait_ld32(r);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (kbase + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
+        mx = fmaxf(mx, swap(mx, 1, ok));
+        st.m = mx * sl2;
+        if (!ok) break;
       }
-      float mx = -INFINITY;
-      const uint64_t l_before = l2;
-      exp_tile(tS, tP, diag, kbase, q_idx, sl2, m_used, l2, mx);
+      st.kr = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < 2; ++cc) {
+        tmem_ld32(tS + 64 * hf + 32 * cc, r);
+        tmem_wait_ld32(r);
+        softmax_chunk(r, tP0 + 16 * cc, tP0, cc, kbase + 32 * cc, q_idx, sl2, diag, st);
+      }
+      // agree on the tile's raise with the other half of the rows
+      const float k_all = fmaxf(st.kr, swap(st.kr, j & 1, ok));
+      if (!ok) break;
+      if (__any_sync(0xffffffffu, k_all > 0.0f)) {
+        tmem_wait_st();
+        const float fp = pow2_neg(k_all - st.kr);     // this half's P and l: from m + kr to m + k_all
+        scale_cols16<true>(tP0, fp);
+        scale_cols16<true>(tP0 + 16, fp);
+        float la, lb;
+        f2_unpack(st.l2, la, lb);
+        st.l2 = f2_pack(la * fp, lb * fp);
+        if (j > 0) {
+          // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(bar(B_ODONE + 2 * w + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, 32));
+          if (!ok) break;
+          tc_fence_after();
+          const float fo = pow2_neg(k_all);
+          scale_cols16<false>(tO, fo);
+          scale_cols16<false>(tO + 16, fo);
+        }
+        st.m += k_all;
+      }
       tmem_wait_st();
-      if (__any_sync(0xffffffffu, mx > 120.0f)) {
-        // a score far above the reference max (only with inputs that are not unit q/k, where
-        // 2^x could overflow): redo this tile from its true max -- S is still in TMEM
-        const float m_new = fmaxf(m_used, max_tile(tS, kbase, q_idx) * sl2);
-        const float f = ex2_approx(m_used - m_new);
-        if (j >= 1) scale_o(tO, f);
-        float la, lb;
-        f2_unpack(l_before, la, lb);
-        l2 = f2_pack(la * f, lb * f);
-        float mx2 = -INFINITY;
-        exp_tile(tS, tP, diag, kbase, q_idx, sl2, m_new, l2, mx2);
-        tmem_wait_st();
-        m_used = m_new;
-      } else if (__any_sync(0xffffffffu, mx > 8.0f)) {
-        // raise the reference max by an integer k so every 2^x <= 2^8: P, O and l scale by 2^-k (exact)
-        const float k = mx > 8.0f ? ceilf(mx) - 8.0f : 0.0f;   // integer in [0, 112]
-        const float f = __int_as_float((127 - (int)k) << 23);    // exactly 2^-k
-        scale_p(tP, f);
-        if (j >= 1) scale_o(tO, f);
-        tmem_wait_st();
-        float la, lb;
-        f2_unpack(l2, la, lb);
-        l2 = f2_pack(la * f, lb * f);
-        m_used += k;
-      }
       tc_fence_before();
-      mbar_arrive(bar(B_TDONE + w));
+      mbar_arrive(bar(B_TDONE + slot));
     }
     if (ok && n_w > 0) {
-      ok = mbar_wait(bar(B_PVDONE + w), (n_w - 1) & 1, abort_flag, 31);
-      ok = __all_sync(0xffffffffu, ok);
+      float la, lb;
+      f2_unpack(st.l2, la, lb);
+      const float l = la + lb;
+      const float l_all = l + swap(l, (n_w & 1), ok);
+      ok = ok && __all_sync(0xffffffffu,
+                            mbar_wait(bar(B_ODONE + 2 * w + ((n_w - 1) & 1)), ((n_w - 1) >> 1) & 1, abort_flag, 31));
       if (ok) {
         tc_fence_after();
-        float la, lb;
-        f2_unpack(l2, la, lb);
-        const float inv_l = 1.0f / (la + lb);
-        __nv_bfloat16* orow = p.o + (int64_t)b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)h * p.os_h;
+        const float inv_l = 1.0f / l_all;
+        uint32_t o[32];
+        tmem_ld32(tO, o);
+        tmem_wait_ld32(o);
+        if (q_idx < p.T) {
+          __nv_bfloat16* orow =
+              p.o + (int64_t)b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)h * p.os_h + 32 * hf;
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tO + c, o);
-          tmem_wait_ld();
-          if (q_idx < p.T) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
-              v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
-              v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
-              v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + c + i) = v;
-            }
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + i) = v;
           }
         }
       }
@@ -705,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMMA) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -769,10 +874,10 @@ static int launch_v2(const void* q, const void* k, const void* v, void* o, int B
   p.scale_log2 = scale * 1.4426950408889634f;
   const int64_t blocks = (int64_t)p.n_qt * B * H;
   ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
-  cudaError_t e = cudaFuncSetAttribute(v2::attn_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       v2::Layout::kDynSmem);
+  auto kern = v2::attn_fwd2_kernel;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, v2::Layout::kDynSmem);
   if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "attention: smem attribute: %s", cudaGetErrorString(e));
-  v2::attn_fwd2_kernel<<<(unsigned)blocks, v2::kThreads, v2::Layout::kDynSmem, st>>>(mq, mk, mv, p);
+  kern<<<(unsigned)blocks, v2::kThreads, v2::Layout::kDynSmem, st>>>(mq, mk, mv, p);
   return check_launch("attention (tcgen05, 2-tile)");
 }
 

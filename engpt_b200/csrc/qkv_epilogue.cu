@@ -43,18 +43,29 @@ __device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t n, int s
   return ((int64_t)(b * a.H + h) * a.T + t) * a.Dh;
 }
 
+// Eight raw elements as loaded (bf16: one 16-byte word), converted to fp32 only when used, so a thread
+// keeps its tokens' rows in few registers and more CTAs (more loads in flight) fit on an SM.
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float* x);
+struct Raw8;
 template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* x) {
-  unpack8(ld_once(p), x);  // coherent load: the output may be written over qkv in place
-}
+struct Raw8<__nv_bfloat16> {
+  uint4 v;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = ld_once(p); }  // coherent: may be in place
+  __device__ __forceinline__ void zero() { v = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void to_float(float* x) const { unpack8(v, x); }
+};
 template <>
-__device__ __forceinline__ void load8<float>(const float* p, float* x) {
-  float4 a = *reinterpret_cast<const float4*>(p);
-  float4 b = *reinterpret_cast<const float4*>(p + 4);
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-}
+struct Raw8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *reinterpret_cast<const float4*>(p + 4);
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void to_float(float* x) const {
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+};
 
 template <typename T>
 __device__ __forceinline__ void store8(T* p, const float* x);
@@ -73,12 +84,13 @@ __device__ __forceinline__ void store8<float>(float* p, const float* x) {
 // with LPR lanes (Dh = 8 * LPR, LPR divides 32) per (s, h) row.  All global
 // loads (the tokens' qkv rows, rho, and the tokens' rotary rows, staged in
 // shared memory) are issued before any is used.  In place is safe: each
-// thread writes only the elements it read, after reading them.
+// thread writes only the elements it read, after reading them.  At most 40
+// registers a thread, so four 384-thread CTAs (d = 1024) share an SM.
 constexpr int kQkvTok = 4;
 constexpr int kQkvMaxHalf = 128;   // rotary pairs staged per token (head_dim <= 256)
 
 template <typename T, int LPR>
-__global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
+__global__ void __launch_bounds__(768, 2) qkv_vec_kernel(QkvArgs a) {
   __shared__ __align__(16) float s_cos[kQkvTok][kQkvMaxHalf];
   __shared__ __align__(16) float s_sin[kQkvTok][kQkvMaxHalf];
   const int ntok = a.B * a.T;
@@ -92,17 +104,16 @@ __global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
   const int b0 = n0 / a.T;
   const int t0 = n0 - b0 * a.T;
 
-  float x[kQkvTok][8];
+  Raw8<T> raw[kQkvTok];
   float rho[kQkvTok];
 #pragma unroll
   for (int k = 0; k < kQkvTok; ++k) {
     const int n = n0 + k;
     if (n < ntok) {
-      load8<T>(reinterpret_cast<const T*>(a.qkv) + ((int64_t)n * 3 * a.H + row) * a.Dh + e0, x[k]);
+      raw[k].load(reinterpret_cast<const T*>(a.qkv) + ((int64_t)n * 3 * a.H + row) * a.Dh + e0);
       rho[k] = a.rho[n];
     } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[k][i] = 0.f;
+      raw[k].zero();
       rho[k] = 1.f;
     }
   }
@@ -117,24 +128,18 @@ __global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
     s_cos[k][pi] = live ? a.cos_tab[(int64_t)t * half + pi] : 1.f;
     s_sin[k][pi] = live ? a.sin_tab[(int64_t)t * half + pi] : 0.f;
   }
-  float scl[8];
-  if (s < 2) {
-    const float* sc = a.qk_scale + (int64_t)h * a.Dh + e0;
-    float4 s0 = *reinterpret_cast<const float4*>(sc);
-    float4 s1 = *reinterpret_cast<const float4*>(sc + 4);
-    scl[0] = s0.x * a.qk_mult; scl[1] = s0.y * a.qk_mult; scl[2] = s0.z * a.qk_mult; scl[3] = s0.w * a.qk_mult;
-    scl[4] = s1.x * a.qk_mult; scl[5] = s1.y * a.qk_mult; scl[6] = s1.z * a.qk_mult; scl[7] = s1.w * a.qk_mult;
-  }
   __syncthreads();
   T* base = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v));
   const int p0 = e0 >> 1;  // first rotary pair of this lane
 #pragma unroll
   for (int k = 0; k < kQkvTok; ++k) {
     const int n = n0 + k;
+    float x[8];
+    raw[k].to_float(x);
     // sum of squares across the LPR lanes of this row (groups are lane-aligned; all lanes take part)
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[k][i] * x[k][i];
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
     for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (n >= ntok) continue;
@@ -143,22 +148,26 @@ __global__ void __launch_bounds__(768) qkv_vec_kernel(QkvArgs a) {
     if (s == 2) {
       const float inv_rho = 1.0f / rho[k];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) outv[i] = x[k][i] * inv_rho;
+      for (int i = 0; i < 8; ++i) outv[i] = x[i] * inv_rho;
     } else {
       float den = sqrtf(ss);
       if (a.eps > 0.f) den = fmaxf(den, rho[k] * a.eps);
       const float inv_den = 1.0f / den;
+      const float* sc = a.qk_scale + (int64_t)h * a.Dh + e0;
+      const float4 sc0 = __ldg(reinterpret_cast<const float4*>(sc));
+      const float4 sc1 = __ldg(reinterpret_cast<const float4*>(sc + 4));
+      const float scl[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float xe = x[k][2 * i], xo = x[k][2 * i + 1];
+        const float xe = x[2 * i], xo = x[2 * i + 1];
         float re = xe, ro = xo;
         if (p0 + i < half) {
           const float c = s_cos[k][p0 + i], sn = s_sin[k][p0 + i];
           re = xe * c - xo * sn;
           ro = xe * sn + xo * c;
         }
-        outv[2 * i] = (re * inv_den) * scl[2 * i];
-        outv[2 * i + 1] = (ro * inv_den) * scl[2 * i + 1];
+        outv[2 * i] = (re * inv_den) * (scl[2 * i] * a.qk_mult);
+        outv[2 * i + 1] = (ro * inv_den) * (scl[2 * i + 1] * a.qk_mult);
       }
     }
     store8<T>(base + out_offset(a, n, s, h) + e0, outv);

@@ -44,17 +44,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep up to `hint_ns` for the phase instead of polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test: has the phase with `parity` completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with `parity` to complete.  Gives up when the
 // shared abort word is set by another role, or after kWaitLimitNs, in which
 // case it records ENGPT_ERR_TIMEOUT(site) and raises the abort word.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
 #pragma unroll 1
-  for (int i = 0; i < 256; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  for (int i = 0; i < 4; ++i)
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
   const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     // another role of this CTA gave up, or another CTA recorded a failure: leave quickly
     if (*abort_flag || *reinterpret_cast<volatile int*>(&g_device_status)) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -137,6 +163,57 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
+// The same two MMAs with the accumulate predicate fixed to true (no setp in the issue loop).
+__device__ __forceinline__ void umma_f16_ss_acc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, 1, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_acc(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, 1, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+
+// Warp-wide forms: every lane of the (converged) warp executes them with the same operands and
+// elect.sync picks the one lane that issues, so the operands can stay in uniform registers.
+__device__ __forceinline__ void umma_f16_ss_w(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_w(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+// Advance a shared-memory descriptor's start address by `bytes` (a multiple of 16).
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
+
 // Arrive on `bar` once all previously issued tcgen05 async ops of this thread completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -177,7 +254,38 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+// wait::ld that also ties the 32 destination registers of the loads it waits
+// for, so the compiler cannot schedule their first use above the wait.
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 "version 1").
@@ -235,32 +343,6 @@ __device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
-}
-__device__ __forceinline__ uint64_t fadd2_rm(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// 2^x for a pair, on the FMA pipe (no MUFU): Cody-Waite split x = n + f with
-// n = floor(x) taken by adding 1.5 * 2^23 with round-toward -inf (n lands in
-// the low mantissa bits), f in [0, 1); 2^f from a degree-3 minimax polynomial
-// (Remez fit of the relative error on [0, 1), max 7.5e-5 = 2^-13.7); 2^n is
-// applied by adding n << 23 to the exponent field.  Valid for x in [-126, 126]
-// (callers clamp the low end).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  const uint64_t kShift = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t t = fadd2_rm(x, kShift);
-  const uint64_t f = fsub2(x, fsub2(t, kShift));
-  uint64_t p = ffma2(f, f2_pack(0x1.3f96a4p-4f, 0x1.3f96a4p-4f), f2_pack(0x1.cefc4cp-3f, 0x1.cefc4cp-3f));
-  p = ffma2(p, f, f2_pack(0x1.64444cp-1f, 0x1.64444cp-1f));
-  p = ffma2(p, f, f2_pack(0x1.fff632p-1f, 0x1.fff632p-1f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  const float r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  const float r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-  return f2_pack(r0, r1);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

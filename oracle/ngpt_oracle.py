@@ -192,10 +192,18 @@ def scaled_logits_from_carried(y: Array, rho: Array, output_emb: Array, logit_sc
     return (y / rho[..., None]) @ (output_emb * logit_scale[:, None]).T
 
 
-def cross_entropy(logits: Array, targets: Array) -> float:
-    """Mean token cross-entropy (engpt/models.py:328-333 via ``F.cross_entropy``)."""
+def cross_entropy(logits: Array, targets: Array, ignore_index: int = -100) -> float:
+    """Mean token cross-entropy (engpt/models.py:328-333 via ``F.cross_entropy``).
+
+    Targets equal to ``ignore_index`` (F.cross_entropy's default -100) are left
+    out of the mean; with no valid target the mean is NaN, as in torch.
+    """
     flat = logits.reshape(-1, logits.shape[-1]).astype(np.float64)
     t = targets.reshape(-1)
+    keep = t != ignore_index
+    if not keep.any():
+        return float("nan")
+    flat, t = flat[keep], t[keep]
     m = flat.max(axis=-1, keepdims=True)
     lse = (m[:, 0] + np.log(np.exp(flat - m).sum(axis=-1)))
     return float(np.mean(lse - flat[np.arange(flat.shape[0]), t]))
