@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--heads", type=int, default=16)
     ap.add_argument("--dim", type=int, default=1024)
     ap.add_argument("--vocab", type=int, default=50257)
+    ap.add_argument("--qkv-layout", choices=["separate", "packed"], default="separate",
+                    help="attention workload: separate [B,T,H,Dh] q/k/v, or views of one [B,T,3,H,Dh] buffer")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -420,6 +422,10 @@ def run_attention(a, world, rank, local_rank):
     q = (q / q.norm(dim=-1, keepdim=True) * s).to(dev, torch.bfloat16)
     k = (k / k.norm(dim=-1, keepdim=True) * s).to(dev, torch.bfloat16)
     v = v.to(dev, torch.bfloat16)
+    if a.qkv_layout == "packed":
+        # q/k/v as views of one [B, T, 3, H, Dh] buffer, the layout the forward's QKV epilogue leaves
+        packed = torch.stack([q, k, v], dim=2).contiguous()
+        q, k, v = packed[:, :, 0], packed[:, :, 1], packed[:, :, 2]
     scale = math.sqrt(Dh)
 
     def ours():
@@ -456,7 +462,7 @@ def run_attention(a, world, rank, local_rank):
         "metric": "isolated nGPT causal attention TFLOP/s", "value": achieved, "unit": "TFLOP/s",
         "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
         "dtype": "bf16", "data": "synthetic (seeded normal q/k/v, unit q/k scaled by U(0.9,1.1))",
-        "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh)",
+        "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh), q/k/v {a.qkv_layout}",
                    "l2": "inputs read once per launch; no flush between launches"},
         "roofline": {"kernel": "attn_fwd2_kernel (tcgen05)" if Dh == 64 else f"attn_fwd_kernel<{Dh}> (tcgen05)", "bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
