@@ -40,6 +40,23 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "forward tokens/sec (EfficientNGPT bf16, L=16 d=1024 H=16 T=2048)"
+
+# The result line goes to the original stdout; everything else written to fd 1 (library banners such as
+# NCCL's version line, stray prints) is redirected to stderr so stdout carries exactly one JSON line.
+_RESULT_OUT = None
+
+
+def emit(obj):
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
+def _guard_stdout():
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 UNIT = "tokens/s"
 
 
@@ -205,13 +222,13 @@ def run_reference(a, world, rank):
     total = sum(times)
     value = a.steps * n * a.seq / total
     sample = f"{n} x {a.seq}-token sequence(s) of the workload per step, fp32 numpy, {cores} threads"
-    print(json.dumps({
+    emit({
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": 1000.0 * total / a.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(a, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -350,7 +367,7 @@ def run_gpu(a, world, rank, local_rank):
                                              f"{dt:.1f} s"}
         except Exception as exc:  # pragma: no cover - reported, not fatal
             out["cpu_baseline"] = {"error": repr(exc)}
-    print(json.dumps(out), flush=True)
+    emit(out)
 
 
 def profile_kernels(model, step, idx, tgt, cfg, a):
@@ -458,7 +475,7 @@ def run_attention(a, world, rank, local_rank):
     flops = 2.0 * B * H * T * T * Dh
     peaks = load_peaks()
     achieved = flops / (ms / 1000.0) / 1e12
-    print(json.dumps({
+    emit({
         "metric": "isolated nGPT causal attention TFLOP/s", "value": achieved, "unit": "TFLOP/s",
         "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
         "dtype": "bf16", "data": "synthetic (seeded normal q/k/v, unit q/k scaled by U(0.9,1.1))",
@@ -469,11 +486,12 @@ def run_attention(a, world, rank, local_rank):
                      "traffic": None, "peak_source": f"{peaks['source']} bf16 burst"},
         "torch_sdpa_bf16": {"ms": ms_torch, "tflops": flops / (ms_torch / 1000.0) / 1e12},
         "clocks": clocks,
-    }), flush=True)
+    })
 
 
 def main():
     a = parse_args()
+    _guard_stdout()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
