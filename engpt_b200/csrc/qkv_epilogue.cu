@@ -79,39 +79,41 @@ __device__ __forceinline__ void store8<float>(float* p, const float* x) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
 }
 
-// A CTA owns kQkvTok consecutive tokens: thread e8 of the 3*d/8 threads owns
-// 8 consecutive elements of each token's [3, H, Dh] slice, i.e. (s, h, sub)
-// with LPR lanes (Dh = 8 * LPR, LPR divides 32) per (s, h) row.  All global
-// loads (the tokens' qkv rows, rho, and the tokens' rotary rows, staged in
-// shared memory) are issued before any is used.  In place is safe: each
-// thread writes only the elements it read, after reading them.  At most 40
-// registers a thread, so four 384-thread CTAs (d = 1024) share an SM.
-constexpr int kQkvTok = 4;
+// A CTA owns kQkvTok consecutive tokens; its threads form an (H * LPR, 3)
+// block: threadIdx.y is q|k|v, threadIdx.x / LPR the head and threadIdx.x % LPR
+// the 8-element slice (Dh = 8 * LPR, LPR a power of two dividing 32), so every
+// index is a shift.  All global loads (the tokens' qkv slices, rho, and the
+// tokens' rotary rows, staged in shared memory) are issued before any is used.
+// The kernel is instruction-bound at HBM speed, so per-token work is kept
+// minimal: scales are loaded once, bf16 results use the MUFU reciprocal forms
+// (about 2 ulp, far below bf16 rounding; fp32 results use IEEE sqrt and
+// division), and an in-place result reuses its load address.  In place is
+// safe: each thread writes only the elements it read, after reading them.
+constexpr int kQkvTok = 2;
 constexpr int kQkvMaxHalf = 128;   // rotary pairs staged per token (head_dim <= 256)
 
 template <typename T, int LPR>
 __global__ void __launch_bounds__(768, 2) qkv_vec_kernel(QkvArgs a) {
   __shared__ __align__(16) float s_cos[kQkvTok][kQkvMaxHalf];
   __shared__ __align__(16) float s_sin[kQkvTok][kQkvMaxHalf];
+  constexpr bool kFast = sizeof(T) == 2;
   const int ntok = a.B * a.T;
   const int n0 = blockIdx.x * kQkvTok;
-  const int e8 = threadIdx.x;                     // < 3 * H * LPR
-  const int row = e8 / LPR;                       // s * H + h
-  const int sub = e8 - row * LPR;
-  const int s = row / a.H;
-  const int h = row - s * a.H;
+  const int s = threadIdx.y;                      // 0: q, 1: k, 2: v
+  const int h = threadIdx.x / LPR;
+  const int sub = threadIdx.x % LPR;
   const int e0 = sub * 8;
-  const int b0 = n0 / a.T;
-  const int t0 = n0 - b0 * a.T;
+  const int row = s * a.H + h;
+  const int64_t tok_stride = (int64_t)3 * a.H * a.Dh;
+  T* src = const_cast<T*>(reinterpret_cast<const T*>(a.qkv)) + ((int64_t)n0 * 3 * a.H + row) * a.Dh + e0;
 
   Raw8<T> raw[kQkvTok];
   float rho[kQkvTok];
 #pragma unroll
   for (int k = 0; k < kQkvTok; ++k) {
-    const int n = n0 + k;
-    if (n < ntok) {
-      raw[k].load(reinterpret_cast<const T*>(a.qkv) + ((int64_t)n * 3 * a.H + row) * a.Dh + e0);
-      rho[k] = a.rho[n];
+    if (n0 + k < ntok) {
+      raw[k].load(src + k * tok_stride);
+      rho[k] = a.rho[n0 + k];
     } else {
       raw[k].zero();
       rho[k] = 1.f;
@@ -119,18 +121,30 @@ __global__ void __launch_bounds__(768, 2) qkv_vec_kernel(QkvArgs a) {
   }
   // rotary rows of the CTA's tokens -> shared memory
   const int half = a.rope_half;
-  for (int i = threadIdx.x; i < kQkvTok * half; i += blockDim.x) {
-    const int k = i / half;
-    const int pi = i - k * half;
-    int t = t0 + k;
-    while (t >= a.T) t -= a.T;  // tokens of the next sequence
-    const bool live = n0 + k < ntok;
-    s_cos[k][pi] = live ? a.cos_tab[(int64_t)t * half + pi] : 1.f;
-    s_sin[k][pi] = live ? a.sin_tab[(int64_t)t * half + pi] : 0.f;
+  const int t0 = n0 % a.T;
+  for (int pi = threadIdx.y * blockDim.x + threadIdx.x; pi < half; pi += blockDim.x * blockDim.y) {
+#pragma unroll
+    for (int k = 0; k < kQkvTok; ++k) {
+      int t = t0 + k;
+      while (t >= a.T) t -= a.T;  // tokens of the next sequence
+      const bool live = n0 + k < ntok;
+      s_cos[k][pi] = live ? a.cos_tab[(int64_t)t * half + pi] : 1.f;
+      s_sin[k][pi] = live ? a.sin_tab[(int64_t)t * half + pi] : 0.f;
+    }
+  }
+  float scl[8];
+  if (s < 2) {
+    const float* sc = a.qk_scale + (int64_t)h * a.Dh + e0;
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + 4));
+    scl[0] = s0.x * a.qk_mult; scl[1] = s0.y * a.qk_mult; scl[2] = s0.z * a.qk_mult; scl[3] = s0.w * a.qk_mult;
+    scl[4] = s1.x * a.qk_mult; scl[5] = s1.y * a.qk_mult; scl[6] = s1.z * a.qk_mult; scl[7] = s1.w * a.qk_mult;
   }
   __syncthreads();
   T* base = reinterpret_cast<T*>(s == 0 ? a.q : (s == 1 ? a.k : a.v));
-  const int p0 = e0 >> 1;  // first rotary pair of this lane
+  const bool inplace = a.layout == ENGPT_QKV_INPLACE;
+  const int p0 = e0 >> 1;      // first rotary pair of this lane (a multiple of 4)
+  const bool rot = p0 < half;  // half is a multiple of 4: a lane's 4 pairs rotate together or not at all
 #pragma unroll
   for (int k = 0; k < kQkvTok; ++k) {
     const int n = n0 + k;
@@ -139,38 +153,42 @@ __global__ void __launch_bounds__(768, 2) qkv_vec_kernel(QkvArgs a) {
     // sum of squares across the LPR lanes of this row (groups are lane-aligned; all lanes take part)
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
 #pragma unroll
     for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (n >= ntok) continue;
     float outv[8];
-    // one reciprocal per row, then multiplies (within 1 ulp of dividing each element)
     if (s == 2) {
-      const float inv_rho = 1.0f / rho[k];
+      const float inv_rho = kFast ? __fdividef(1.0f, rho[k]) : 1.0f / rho[k];
 #pragma unroll
       for (int i = 0; i < 8; ++i) outv[i] = x[i] * inv_rho;
     } else {
-      float den = sqrtf(ss);
-      if (a.eps > 0.f) den = fmaxf(den, rho[k] * a.eps);
-      const float inv_den = 1.0f / den;
-      const float* sc = a.qk_scale + (int64_t)h * a.Dh + e0;
-      const float4 sc0 = __ldg(reinterpret_cast<const float4*>(sc));
-      const float4 sc1 = __ldg(reinterpret_cast<const float4*>(sc + 4));
-      const float scl[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
+      // 1 / max(|q|, rho*eps): one reciprocal per row, then multiplies
+      float inv_den;
+      if (kFast) {
+        inv_den = rsqrtf(ss);
+        if (a.eps > 0.f) inv_den = fminf(inv_den, __fdividef(1.0f, rho[k] * a.eps));
+      } else {
+        float den = sqrtf(ss);
+        if (a.eps > 0.f) den = fmaxf(den, rho[k] * a.eps);
+        inv_den = 1.0f / den;
+      }
+      if (rot) {
+        const float4 c4 = *reinterpret_cast<const float4*>(&s_cos[k][p0]);
+        const float4 s4 = *reinterpret_cast<const float4*>(&s_sin[k][p0]);
+        const float c[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float xe = x[2 * i], xo = x[2 * i + 1];
-        float re = xe, ro = xo;
-        if (p0 + i < half) {
-          const float c = s_cos[k][p0 + i], sn = s_sin[k][p0 + i];
-          re = xe * c - xo * sn;
-          ro = xe * sn + xo * c;
+        for (int i = 0; i < 4; ++i) {
+          const float xe = x[2 * i], xo = x[2 * i + 1];
+          outv[2 * i] = ((xe * c[i] - xo * sn[i]) * inv_den) * scl[2 * i];
+          outv[2 * i + 1] = ((xe * sn[i] + xo * c[i]) * inv_den) * scl[2 * i + 1];
         }
-        outv[2 * i] = (re * inv_den) * (scl[2 * i] * a.qk_mult);
-        outv[2 * i + 1] = (ro * inv_den) * (scl[2 * i + 1] * a.qk_mult);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) outv[i] = (x[i] * inv_den) * scl[i];
       }
     }
-    store8<T>(base + out_offset(a, n, s, h) + e0, outv);
+    store8<T>(inplace ? src + k * tok_stride : base + out_offset(a, n, s, h) + e0, outv);
   }
 }
 
@@ -260,7 +278,7 @@ extern "C" int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rh
   cudaStream_t st = as_stream(stream);
   const int esz = dtype == ENGPT_BF16 ? 2 : 4;
   const bool vec_ok = (Dh == 8 || Dh == 16 || Dh == 32 || Dh == 64 || Dh == 128 || Dh == 256) &&
-                      rope_half <= kQkvMaxHalf &&
+                      rope_half <= kQkvMaxHalf && rope_half % 4 == 0 &&
                       aligned(qkv, 16) && aligned(q_out, 16) && aligned(k_out, 16) && aligned(v_out, 16) &&
                       aligned(qk_scale, 16) && (rope_half == 0 || (aligned(cos_tab, 16) && aligned(sin_tab, 16))) &&
                       ((int64_t)Dh * esz) % 16 == 0;
@@ -272,9 +290,9 @@ extern "C" int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rh
 #define ENGPT_QKV_LAUNCH(L)                                                                                  \
   case L:                                                                                                    \
     if (dtype == ENGPT_BF16)                                                                                 \
-      qkv_vec_kernel<__nv_bfloat16, L><<<(unsigned)blocks, threads_per_token, 0, st>>>(a);                   \
+      qkv_vec_kernel<__nv_bfloat16, L><<<(unsigned)blocks, dim3(H * L, 3), 0, st>>>(a);                       \
     else                                                                                                     \
-      qkv_vec_kernel<float, L><<<(unsigned)blocks, threads_per_token, 0, st>>>(a);                           \
+      qkv_vec_kernel<float, L><<<(unsigned)blocks, dim3(H * L, 3), 0, st>>>(a);                               \
     break;
     switch (lpr) {
       ENGPT_QKV_LAUNCH(1)
