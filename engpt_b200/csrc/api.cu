@@ -235,23 +235,33 @@ __global__ void __launch_bounds__(256) cast_many_kernel(const __grid_constant__ 
 }
 
 // ------------------------------------------------------------ cross-entropy
-// One CTA per row.  Online (max, sum-exp) per thread, then a CTA combine.
+// Log-sum-exp state in base 2: m = running max of x * log2(e), s = sum of 2^(x * log2(e) - m).
+// The running max is raised only when a value exceeds it, so the common step is one FFMA and one
+// MUFU ex2 per logit.
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void lse_push(float& m, float& s, float x) {
-  if (x > m) {
-    s = s * __expf(m - x) + 1.0f;
-    m = x;
+  const float xl = x * kLog2e;
+  if (xl > m) {
+    s = s * ex2_fast(m - xl) + 1.0f;
+    m = xl;
   } else {
-    s += __expf(x - m);
+    s += ex2_fast(xl - m);
   }
 }
-
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
-  float mm = fmaxf(m, m2);
+  const float mm = fmaxf(m, m2);
   if (mm == -INFINITY) return;
-  s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
+  s = s * ex2_fast(m - mm) + s2 * ex2_fast(m2 - mm);
   m = mm;
 }
 
+// One CTA per row: online log-sum-exp over the row (16-byte loads for bf16), then the
+// target's term.  ignore_index (-100) rows contribute 0.
 template <typename T>
 __global__ void __launch_bounds__(256) cross_entropy_rows_kernel(const T* __restrict__ logits, int64_t rows,
                                                                  int64_t vocab, int64_t ld,
@@ -273,13 +283,20 @@ __global__ void __launch_bounds__(256) cross_entropy_rows_kernel(const T* __rest
     for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
       float x[8];
       unpack8(ld_stream(body + v), x);
-      float cm = x[0];
+      float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
+      const float cml = cm * kLog2e;
+      if (cml > m) {   // rare after the first few vectors of a thread
+        s *= ex2_fast(m - cml);
+        m = cml;
+      }
+      const float nm = -m;
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int i = 1; i < 8; ++i) cm = fmaxf(cm, x[i]);
-      float cs = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cs += __expf(x[i] - cm);
-      lse_merge(m, s, cm, cs);
+      for (int i = 0; i < 8; i += 2) {
+        s0 += ex2_fast(fmaf(x[i], kLog2e, nm));
+        s1 += ex2_fast(fmaf(x[i + 1], kLog2e, nm));
+      }
+      s += s0 + s1;
     }
     for (int64_t c = head + nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) lse_push(m, s, load_as_f32(row, c));
   } else {
@@ -310,7 +327,7 @@ __global__ void __launch_bounds__(256) cross_entropy_rows_kernel(const T* __rest
       record_device_error(ENGPT_ERR_ARG, 2);
       loss = NAN;
     } else {
-      loss = (M + logf(S)) - load_as_f32(row, t);
+      loss = (M + log2f(S)) * 0.6931471805599453f - load_as_f32(row, t);   // logsumexp - logit[t]
     }
     row_loss[r] = loss;
   }
