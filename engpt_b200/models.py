@@ -13,8 +13,8 @@ forward (engpt/models.py:263-292) on the GPU:
     attn     = causal attention  -> [B,T,H,Dh]           engpt_causal_attention (tcgen05)
     branch   = attn @ W_o^T                              cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y/rho engpt_carried_residual_gauge
-    ug       = (Y/rho)_bf16 @ W_ug^T                     cuBLAS
-    hidden   = SwiGLU epilogue                           engpt_swiglu
+    hidden   = SwiGLU((Y/rho)_bf16 @ W_ug^T)             engpt_up_gate_swiglu (tcgen05 GEMM, fused epilogue;
+                                                         fp32 mode: cuBLAS + engpt_swiglu)
     branch   = hidden @ W_down^T                         cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y    engpt_carried_residual_gauge
   logits = (Y/rho)_bf16 @ (E_out * s_z_eff)^T_bf16       engpt_scale_rows_cast + cuBLAS
@@ -126,12 +126,13 @@ class EfficientNGPTBlock(nn.Module):
 class _Workspace:
     """Activation buffers for one (batch, seq_len, precision) shape on one device."""
 
-    def __init__(self, cfg: ModelConfig, bsz: int, seq_len: int, device: torch.device, bf16: bool):
+    def __init__(self, cfg: ModelConfig, bsz: int, seq_len: int, device: torch.device, bf16: bool,
+                 fuse_mlp: bool = True):
         d, H, Dh, W = cfg.n_embd, cfg.n_head, cfg.head_dim, cfg.mlp_width
         n = bsz * seq_len
         act = torch.bfloat16 if bf16 else torch.float32
         e = lambda *shape, dtype=act: torch.empty(*shape, device=device, dtype=dtype)  # noqa: E731
-        self.key = (bsz, seq_len, bf16, device)
+        self.key = (bsz, seq_len, bf16, device, fuse_mlp)
         self.bsz, self.seq_len, self.n = bsz, seq_len, n
         self.act = act
         self.y = e(n, d, dtype=torch.float32)
@@ -143,7 +144,9 @@ class _Workspace:
         self.q, self.k, self.v = qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2]   # [B, T, H, Dh] views
         self.attn = e(n, d)                   # [B, T, H, Dh]
         self.branch = e(n, d)
-        self.ug = e(n, 2 * W)
+        # bf16 mode fuses SwiGLU into the up/gate GEMM (no [n, 2W] buffer); fp32 mode runs cuBLAS + the
+        # SwiGLU kernel
+        self.ug = None if (bf16 and fuse_mlp and W % 128 == 0 and d % 8 == 0) else e(n, 2 * W)
         self.hidden = e(n, W)
         self.row_loss = e(n, dtype=torch.float32)
         self.cos = e(seq_len, Dh // 2, dtype=torch.float32)
@@ -180,6 +183,8 @@ class EfficientNGPT(nn.Module):
         self.project_parameters_()
         self._ws: Optional[_Workspace] = None
         self.attn_impl = _lib.ATTN_AUTO
+        # bf16 mode: up/gate projection and SwiGLU in one tcgen05 GEMM (False: cuBLAS + SwiGLU kernel)
+        self.fuse_mlp = True
         # False: logits are a strided [B, T, V] view of a [N, V rounded up to 64] buffer (no copy);
         # True: a contiguous copy is returned
         self.contiguous_logits = False
@@ -254,10 +259,10 @@ class EfficientNGPT(nn.Module):
         return loss
 
     def _workspace(self, bsz: int, seq_len: int, device: torch.device, bf16: bool) -> _Workspace:
-        key = (bsz, seq_len, bf16, device)
+        key = (bsz, seq_len, bf16, device, self.fuse_mlp)
         if self._ws is None or self._ws.key != key:
             self._ws = None
-            self._ws = _Workspace(self.cfg, bsz, seq_len, device, bf16)
+            self._ws = _Workspace(self.cfg, bsz, seq_len, device, bf16, self.fuse_mlp)
         return self._ws
 
     def release_workspace(self) -> None:
@@ -348,9 +353,16 @@ class EfficientNGPT(nn.Module):
                           act, blk.alpha_attn_raw.data_ptr(), float(blk.alpha_mult), 1, float(cfg.norm_eps),
                           float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(),
                           ws.rho.data_ptr(), ws.x.data_ptr(), _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H, st)
-                torch.mm(ws.x, wug.t(), out=ws.ug)
-                _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, blk.s_u.data_ptr(), blk.s_gate.data_ptr(),
-                          float(u_mult), float(sqrt_d), n, W, ws.hidden.data_ptr(), act, st)
+                if ws.ug is None:
+                    # up/gate GEMM with the SwiGLU epilogue fused (tcgen05): the [n, 2W] projection never
+                    # leaves TMEM
+                    _lib.call("engpt_up_gate_swiglu", ws.x.data_ptr(), wug.data_ptr(), blk.s_u.data_ptr(),
+                              blk.s_gate.data_ptr(), float(u_mult), float(sqrt_d), n, d, W,
+                              ws.hidden.data_ptr(), st)
+                else:
+                    torch.mm(ws.x, wug.t(), out=ws.ug)
+                    _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, blk.s_u.data_ptr(), blk.s_gate.data_ptr(),
+                              float(u_mult), float(sqrt_d), n, W, ws.hidden.data_ptr(), act, st)
                 torch.mm(ws.hidden, wd.t(), out=ws.branch)
                 if i < last:
                     aux_mode = _lib.AUX_BF16_Y if bf16 else _lib.AUX_NONE

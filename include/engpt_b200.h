@@ -168,6 +168,39 @@ ENGPT_API int engpt_cast_f32_bf16_many(const void* const* src, void* const* dst,
                                        void* stream);
 
 /*
+ * Dense projection -- the bias-free F.linear of engpt/models.py:142,152,166,172
+ * (nn.Linear under bf16 autocast): C[M, N] = A[M, K] * B[N, K]^T, bf16 A, B
+ * (rows of K contiguous elements, row strides lda / ldb) and bf16 C (row
+ * stride ldc), fp32 accumulation.  Persistent tcgen05 kernel; rows 16-byte
+ * aligned, K a multiple of 8.
+ */
+ENGPT_API int engpt_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int M,
+                              int N, int K, void* stream);
+
+/*
+ * QKV projection with the QKV post-process fused into the GEMM epilogue --
+ * F.linear of engpt/models.py:142 followed by qkv_postprocess_from_carried
+ * (engpt/kernels.py:139-179) on the fp32 accumulator: x [B*T, d] bf16,
+ * w_qkv [3d, d] bf16; writes the post-processed q | k | v rows into qkv_out
+ * [B*T, 3, H, Dh] bf16 (the layout engpt_qkv_postprocess leaves in place).
+ * head_dim 64, d a multiple of 256.
+ */
+ENGPT_API int engpt_qkv_projection(const void* x, const void* w_qkv, const float* rho, const float* cos_tab,
+                                   const float* sin_tab, int rope_half, const float* qk_scale, float qk_mult,
+                                   float norm_eps, int B, int T, int H, int Dh, void* qkv_out, void* stream);
+
+/*
+ * Up/gate projection with SwiGLU fused into the GEMM epilogue --
+ * carried_up_gate_swiglu (engpt/kernels.py:182-206) from x = bf16(Y / rho):
+ * w_ug [2 * width, d] bf16 (u rows, then gate rows, as nn.Linear stores them),
+ * hidden [rows, width] bf16 = (u * s_u * u_mult) * silu(gate * s_gate *
+ * gate_mult), computed from the fp32 accumulator.  width a multiple of 128.
+ */
+ENGPT_API int engpt_up_gate_swiglu(const void* x, const void* w_ug, const float* s_u, const float* s_gate,
+                                   float u_mult, float gate_mult, int64_t rows, int d, int width, void* hidden,
+                                   void* stream);
+
+/*
  * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).
  * logits [rows, vocab] with leading dimension ld (elements), `dtype`;
  * targets int64 [rows].  row_loss [rows] fp32 is caller-provided scratch;
