@@ -405,6 +405,11 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
         "engpt_embed_carried": (4 + 4 + 2) * n * d + 12 * n,
         "engpt_cast_f32_bf16_many": 6 * 16 * a.layers * d * d,            # fp32 weights in, bf16 out
     }
+    W = 4 * d
+    flops = {   # tensor-bound fused GEMMs: 2 * M * N * K
+        "engpt_qkv_projection": 2.0 * n * 3 * d * d,
+        "engpt_up_gate_swiglu": 2.0 * n * 2 * W * d,
+    }
     out = {}
     for name, evs in per.items():
         ms = [e0.elapsed_time(e1) for e0, e1 in evs]
@@ -414,6 +419,10 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
             gbs = alg[name] / (avg / 1000.0) / 1e9
             rec.update({"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"],
                         "bytes_per_launch": alg[name]})
+        elif name in flops:
+            tf = flops[name] / (avg / 1000.0) / 1e12
+            rec.update({"bound": "tensor", "achieved_tflops": tf, "frac": tf / peaks["bf16_tflops_sustained"],
+                        "flops_per_launch": flops[name]})
         out[name.replace("engpt_", "")] = rec
     return out
 

@@ -113,52 +113,75 @@ struct QkvEpi {
   int M, T, d, rope_half;
   __device__ __forceinline__ void tile(int m, int tn, uint32_t tacc) const {
     const int col0 = tn * BN;
-    const int part = col0 / d;            // 0: q, 1: k, 2: v
+    const int part = col0 / d;            // 0: q, 1: k, 2: v (a 256-column tile lies inside one)
     const bool live = m < M;
     const float rho_m = live ? __ldg(rho + m) : 1.f;
-    const int t = live ? m % T : 0;
+    __nv_bfloat16* dst_row = out + (int64_t)(live ? m : 0) * (3 * d) + col0;
+    if (part == 2) {
+      const float inv = __fdividef(1.0f, rho_m);
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 32) {
+        float x[32];
+        load_acc32(tacc + cc, x);
+        if (!live) continue;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          float o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = x[i + k] * inv;
+          *reinterpret_cast<uint4*>(dst_row + cc + i) = pack8(o);
+        }
+      }
+      return;
+    }
+    // this token's rotary row, once for the tile's four heads (pairs >= rope_half: cos 1, sin 0)
+    float cs[32], sn[32];
+    {
+      const int t = live ? m % T : 0;
+      const float* crow = cos_tab + (int64_t)t * rope_half;
+      const float* srow = sin_tab + (int64_t)t * rope_half;
+      if (rope_half == 32) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(crow + i));
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(srow + i));
+          cs[i] = c4.x; cs[i + 1] = c4.y; cs[i + 2] = c4.z; cs[i + 3] = c4.w;
+          sn[i] = s4.x; sn[i + 1] = s4.y; sn[i + 2] = s4.z; sn[i + 3] = s4.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          cs[i] = i < rope_half ? __ldg(crow + i) : 1.f;
+          sn[i] = i < rope_half ? __ldg(srow + i) : 0.f;
+        }
+      }
+    }
 #pragma unroll 1
     for (int hh = 0; hh < BN / 64; ++hh) {
       float x[64];
       load_acc32(tacc + 64 * hh, x);
       load_acc32(tacc + 64 * hh + 32, x + 32);
       if (!live) continue;
-      const int col = col0 + 64 * hh;
-      __nv_bfloat16* dst = out + (int64_t)m * (3 * d) + col;
-      if (part == 2) {
-        const float inv = __fdividef(1.0f, rho_m);
-#pragma unroll
-        for (int i = 0; i < 64; i += 8) {
-          float o[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) o[k] = x[i + k] * inv;
-          *reinterpret_cast<uint4*>(dst + i) = pack8(o);
-        }
-        continue;
-      }
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) ss = fmaf(x[i], x[i], ss);
       float inv_den = rsqrtf(ss);
       if (eps > 0.f) inv_den = fminf(inv_den, __fdividef(1.0f, rho_m * eps));
-      const float* sc = qk_scale + (col - part * d);   // [h, 0..63]
-      const float* cs = cos_tab + (int64_t)t * rope_half;
-      const float* sn = sin_tab + (int64_t)t * rope_half;
+      const float* sc = qk_scale + (col0 + 64 * hh - part * d);   // s_qk[h, 0..63]
+      __nv_bfloat16* dst = dst_row + 64 * hh;
 #pragma unroll
       for (int i = 0; i < 64; i += 8) {
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc + i));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + i + 4));
+        const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float f = inv_den * qk_mult;
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; k += 2) {
           const int pi = (i + k) >> 1;
-          float xe = x[i + k], xo = x[i + k + 1];
-          if (pi < rope_half) {
-            const float c = __ldg(cs + pi), sv = __ldg(sn + pi);
-            const float re = xe * c - xo * sv, ro = xe * sv + xo * c;
-            xe = re;
-            xo = ro;
-          }
-          o[k] = (xe * inv_den) * (__ldg(sc + i + k) * qk_mult);
-          o[k + 1] = (xo * inv_den) * (__ldg(sc + i + k + 1) * qk_mult);
+          const float xe = x[i + k], xo = x[i + k + 1];
+          o[k] = ((xe * cs[pi] - xo * sn[pi]) * f) * scl[k];
+          o[k + 1] = ((xe * sn[pi] + xo * cs[pi]) * f) * scl[k + 1];
         }
         *reinterpret_cast<uint4*>(dst + i) = pack8(o);
       }

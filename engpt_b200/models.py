@@ -8,8 +8,8 @@ random draws).  ``forward`` / ``forward_carried`` run the carried-radius
 forward (engpt/models.py:263-292) on the GPU:
 
   per block (engpt/models.py:140-182)
-    qkv      = Y_bf16 @ W_qkv^T                          cuBLAS (plain GEMM)
-    q, k, v  = fused QKV epilogue, in place over qkv     engpt_qkv_postprocess
+    q, k, v  = post-process(Y_bf16 @ W_qkv^T)            engpt_qkv_projection (tcgen05 GEMM, fused epilogue;
+                                                         otherwise cuBLAS + engpt_qkv_postprocess in place)
     attn     = causal attention  -> [B,T,H,Dh]           engpt_causal_attention (tcgen05)
     branch   = attn @ W_o^T                              cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y/rho engpt_carried_residual_gauge
@@ -185,6 +185,9 @@ class EfficientNGPT(nn.Module):
         self.attn_impl = _lib.ATTN_AUTO
         # bf16 mode: up/gate projection and SwiGLU in one tcgen05 GEMM (False: cuBLAS + SwiGLU kernel)
         self.fuse_mlp = True
+        # bf16 mode, head_dim 64: QKV projection and its post-process in one tcgen05 GEMM (False: cuBLAS +
+        # the QKV epilogue kernel in place)
+        self.fuse_qkv = True
         # False: logits are a strided [B, T, V] view of a [N, V rounded up to 64] buffer (no copy);
         # True: a contiguous copy is returned
         self.contiguous_logits = False
@@ -337,10 +340,18 @@ class EfficientNGPT(nn.Module):
                 else:
                     wq, wo, wug, wd = blk.qkv.weight, blk.out_proj.weight, blk.up_gate.weight, blk.down_proj.weight
                     x_in = ws.y
-                torch.mm(x_in, wq.t(), out=ws.qkv)
-                _lib.call("engpt_qkv_postprocess", ws.qkv.data_ptr(), act, ws.rho.data_ptr(), ws.cos.data_ptr(),
-                          ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(), float(blk.qk_mult), float(cfg.norm_eps),
-                          bsz, seq_len, H, Dh, None, None, None, _lib.QKV_INPLACE, st)
+                if bf16 and self.fuse_qkv and Dh == 64 and d % 256 == 0:
+                    # QKV GEMM with the post-process fused into its epilogue (tcgen05): q|k|v rows are
+                    # written post-processed into the same [n, 3, H, Dh] buffer
+                    _lib.call("engpt_qkv_projection", x_in.data_ptr(), wq.data_ptr(), ws.rho.data_ptr(),
+                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(),
+                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, H, Dh, ws.qkv.data_ptr(), st)
+                else:
+                    torch.mm(x_in, wq.t(), out=ws.qkv)
+                    _lib.call("engpt_qkv_postprocess", ws.qkv.data_ptr(), act, ws.rho.data_ptr(),
+                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(),
+                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, H, Dh, None, None, None,
+                              _lib.QKV_INPLACE, st)
                 if self.attn_timer is not None:
                     self.attn_timer("start")
                 _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
