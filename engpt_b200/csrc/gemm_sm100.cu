@@ -38,10 +38,13 @@ constexpr int kThreads = 192;
 constexpr int kABytes = BM * BK * 2;   // 16 KB
 constexpr int kBBytes = BN * BK * 2;   // 32 KB
 
+constexpr int kOutBytes = BM * 64 * 2;   // one 64-column bf16 output chunk of the tile (16 KB)
+
 struct Layout {
   static constexpr int A = 0;
   static constexpr int B = A + kStages * kABytes;
-  static constexpr int BAR = B + kStages * kBBytes;
+  static constexpr int OUT = B + kStages * kBBytes;        // 2 output staging buffers
+  static constexpr int BAR = OUT + 2 * kOutBytes;
   static constexpr int kBars = 16;
   static constexpr int MISC = BAR + kBars * 8;
   static constexpr int TOTAL = MISC + 16;
@@ -62,8 +65,33 @@ struct Shape {
   int b0, b1, b_step;
 };
 
-// Epilogues.  tile(m, tn, tacc) runs on every epilogue thread for output row m of tile column tn; tacc is
-// the TMEM address of this thread's accumulator row (column 0 of the 256).
+// Output staging: each epilogue thread writes its row's 64 bf16 results of one output chunk (128 bytes)
+// into a 128B-swizzled shared buffer; one thread then stores the 64 x 128 box with TMA (clipped at the
+// tensor's end), so the global writes are full lines instead of 32 scattered rows per warp instruction.
+// Two buffers alternate; a buffer is rewritten only after the store that read it has finished reading.
+struct OutStage {
+  uint8_t* buf;            // 2 x kOutBytes
+  uint32_t sbuf;
+  const CUtensorMap* map;
+  int r;                   // this thread's row in the tile
+  bool leader;             // issues the stores
+  int count;
+  __device__ __forceinline__ void put(int col, int row0, const uint4* v8) {
+    const int b = count & 1;
+    if (leader) bulk_wait_group_read<1>();
+    bar_sync_named(1, 128);
+    uint8_t* rowp = buf + b * kOutBytes + r * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(rowp + ((j ^ (r & 7)) << 4)) = v8[j];
+    fence_proxy_async_smem();
+    bar_sync_named(1, 128);
+    if (leader) {
+      tma_store_2d(map, col, row0, sbuf + b * kOutBytes);
+      bulk_commit_group();
+    }
+    ++count;
+  }
+};
 
 __device__ __forceinline__ void load_acc32(uint32_t taddr, float* v) {
   uint32_t r[32];
@@ -73,27 +101,21 @@ __device__ __forceinline__ void load_acc32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Epilogues: tile(m0, m, tn, tacc, out) runs on every epilogue thread for row m = m0 + r of tile column tn;
+// tacc is the TMEM address of this thread's accumulator row (column 0 of the 256).
+
 // Plain bf16 output: C[m, 256 tn + c] = acc[c].
 struct StoreBf16 {
-  __nv_bfloat16* c;
-  int64_t ldc;
-  int M, N;
-  __device__ __forceinline__ void tile(int m, int tn, uint32_t tacc) const {
+  __device__ __forceinline__ void tile(int m0, int m, int tn, uint32_t tacc, OutStage& out) const {
 #pragma unroll 1
-    for (int cc = 0; cc < BN; cc += 32) {
-      float v[32];
-      load_acc32(tacc + cc, v);
-      const int n0 = tn * BN + cc;
-      if (m >= M) continue;
-      __nv_bfloat16* row = c + (int64_t)m * ldc + n0;
-      if (n0 + 32 <= N) {
+    for (int oc = 0; oc < BN / 64; ++oc) {
+      float v[64];
+      load_acc32(tacc + 64 * oc, v);
+      load_acc32(tacc + 64 * oc + 32, v + 32);
+      uint4 o[8];
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(row + i) = pack8(v + i);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (n0 + i < N) row[i] = __float2bfloat16_rn(v[i]);
-      }
+      for (int j = 0; j < 8; ++j) o[j] = pack8(v + 8 * j);
+      out.put(tn * BN + 64 * oc, m0, o);
     }
   }
 };
@@ -104,33 +126,30 @@ struct StoreBf16 {
 // v is divided by rho.  Written bf16 into the packed [M, 3, H, Dh] rows that the attention kernel reads.
 // Needs Dh = 64 and d a multiple of 256 (a 256-column tile is 4 whole heads of one of q, k, v).
 struct QkvEpi {
-  __nv_bfloat16* out;        // [M, 3d]
   const float* rho;          // [M]
   const float* cos_tab;      // [T, rope_half]
   const float* sin_tab;
   const float* qk_scale;     // [H, Dh]
   float qk_mult, eps;
   int M, T, d, rope_half;
-  __device__ __forceinline__ void tile(int m, int tn, uint32_t tacc) const {
+  __device__ __forceinline__ void tile(int m0, int m, int tn, uint32_t tacc, OutStage& out) const {
     const int col0 = tn * BN;
     const int part = col0 / d;            // 0: q, 1: k, 2: v (a 256-column tile lies inside one)
     const bool live = m < M;
     const float rho_m = live ? __ldg(rho + m) : 1.f;
-    __nv_bfloat16* dst_row = out + (int64_t)(live ? m : 0) * (3 * d) + col0;
     if (part == 2) {
       const float inv = __fdividef(1.0f, rho_m);
 #pragma unroll 1
-      for (int cc = 0; cc < BN; cc += 32) {
-        float x[32];
-        load_acc32(tacc + cc, x);
-        if (!live) continue;
+      for (int hh = 0; hh < BN / 64; ++hh) {
+        float x[64];
+        load_acc32(tacc + 64 * hh, x);
+        load_acc32(tacc + 64 * hh + 32, x + 32);
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          float o[8];
+        for (int i = 0; i < 64; ++i) x[i] *= inv;
+        uint4 o[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) o[k] = x[i + k] * inv;
-          *reinterpret_cast<uint4*>(dst_row + cc + i) = pack8(o);
-        }
+        for (int j = 0; j < 8; ++j) o[j] = pack8(x + 8 * j);
+        out.put(col0 + 64 * hh, m0, o);
       }
       return;
     }
@@ -161,30 +180,30 @@ struct QkvEpi {
       float x[64];
       load_acc32(tacc + 64 * hh, x);
       load_acc32(tacc + 64 * hh + 32, x + 32);
-      if (!live) continue;
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) ss = fmaf(x[i], x[i], ss);
       float inv_den = rsqrtf(ss);
       if (eps > 0.f) inv_den = fminf(inv_den, __fdividef(1.0f, rho_m * eps));
+      const float f = inv_den * qk_mult;
       const float* sc = qk_scale + (col0 + 64 * hh - part * d);   // s_qk[h, 0..63]
-      __nv_bfloat16* dst = dst_row + 64 * hh;
+      uint4 o[8];
 #pragma unroll
       for (int i = 0; i < 64; i += 8) {
         const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc + i));
         const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + i + 4));
         const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const float f = inv_den * qk_mult;
-        float o[8];
+        float v[8];
 #pragma unroll
         for (int k = 0; k < 8; k += 2) {
           const int pi = (i + k) >> 1;
           const float xe = x[i + k], xo = x[i + k + 1];
-          o[k] = ((xe * cs[pi] - xo * sn[pi]) * f) * scl[k];
-          o[k + 1] = ((xe * sn[pi] + xo * cs[pi]) * f) * scl[k + 1];
+          v[k] = ((xe * cs[pi] - xo * sn[pi]) * f) * scl[k];
+          v[k + 1] = ((xe * sn[pi] + xo * cs[pi]) * f) * scl[k + 1];
         }
-        *reinterpret_cast<uint4*>(dst + i) = pack8(o);
+        o[i / 8] = pack8(v);
       }
+      out.put(col0 + 64 * hh, m0, o);
     }
   }
 };
@@ -192,39 +211,47 @@ struct QkvEpi {
 // Up/gate projection + SwiGLU (engpt/kernels.py:182-206): accumulator columns 0-127 are u and 128-255 the
 // gate for hidden columns 128 tn .. 128 tn + 127:  hidden = (u * s_u * u_mult) * silu(gate * s_gate * gate_mult).
 struct SwiGluEpi {
-  __nv_bfloat16* hidden;     // [M, width]
   const float* s_u;
   const float* s_gate;
   float u_mult, gate_mult;
-  int M, width;
-  __device__ __forceinline__ void tile(int m, int tn, uint32_t tacc) const {
+  __device__ __forceinline__ void tile(int m0, int m, int tn, uint32_t tacc, OutStage& out) const {
 #pragma unroll 1
-    for (int cc = 0; cc < 128; cc += 32) {
-      float u[32], g[32];
-      load_acc32(tacc + cc, u);
-      load_acc32(tacc + 128 + cc, g);
-      if (m >= M) continue;
-      const int c0 = tn * 128 + cc;
-      __nv_bfloat16* dst = hidden + (int64_t)m * width + c0;
+    for (int oc = 0; oc < 2; ++oc) {
+      const int c0 = tn * 128 + 64 * oc;
+      uint4 o[8];
 #pragma unroll
-      for (int i = 0; i < 32; i += 8) {
-        float o[8];
+      for (int half = 0; half < 2; ++half) {
+        float u[32], g[32];
+        load_acc32(tacc + 64 * oc + 32 * half, u);
+        load_acc32(tacc + 128 + 64 * oc + 32 * half, g);
+        const int cb = c0 + 32 * half;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float uu = (u[i + k] * __ldg(s_u + c0 + i + k)) * u_mult;
-          const float gg = (g[i + k] * __ldg(s_gate + c0 + i + k)) * gate_mult;
-          o[k] = uu * __fdividef(gg, 1.0f + __expf(-gg));
+        for (int i = 0; i < 32; i += 8) {
+          const float4 su0 = __ldg(reinterpret_cast<const float4*>(s_u + cb + i));
+          const float4 su1 = __ldg(reinterpret_cast<const float4*>(s_u + cb + i + 4));
+          const float4 sg0 = __ldg(reinterpret_cast<const float4*>(s_gate + cb + i));
+          const float4 sg1 = __ldg(reinterpret_cast<const float4*>(s_gate + cb + i + 4));
+          const float su[8] = {su0.x, su0.y, su0.z, su0.w, su1.x, su1.y, su1.z, su1.w};
+          const float sg[8] = {sg0.x, sg0.y, sg0.z, sg0.w, sg1.x, sg1.y, sg1.z, sg1.w};
+          float v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float uu = (u[i + k] * su[k]) * u_mult;
+            const float gg = (g[i + k] * sg[k]) * gate_mult;
+            v[k] = uu * __fdividef(gg, 1.0f + __expf(-gg));
+          }
+          o[4 * half + i / 8] = pack8(v);
         }
-        *reinterpret_cast<uint4*>(dst + i) = pack8(o);
       }
+      out.put(c0, m0, o);
     }
   }
 };
 
 template <typename Epi>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Shape sh,
-                const Epi epi) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const Shape sh, const Epi epi) {
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -329,18 +356,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = warp & 3;                    // TMEM lane quarter of this warp
     const int r = wq * 32 + lane;               // row within the tile
     const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
+    OutStage out{smem + L::OUT, sbase + L::OUT, &tmC, r, threadIdx.x == 64, 0};
+    if (out.leader) tma_prefetch_desc(&tmC);
     for (int i = 0; i < my_tiles; ++i) {
       const int ab = i & 1;
       const int t = blockIdx.x + i * gridDim.x;
       const int m0 = (t / sh.tiles_n) * BM;
       const int tn = t % sh.tiles_n;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ACC_FULL + ab), (i >> 1) & 1, abort_flag, 54));
-      if (!ok) break;
+      const bool ok = mbar_wait(bar(B_ACC_FULL + ab), (i >> 1) & 1, abort_flag, 54);
+      if (bar_red_or(1, 128, !ok)) break;     // the four epilogue warps leave together
       tc_fence_after();
-      epi.tile(m0 + r, tn, tmem + BN * ab + t_lane);
+      epi.tile(m0, m0 + r, tn, tmem + BN * ab + t_lane, out);
       tc_fence_before();
       mbar_arrive(bar(B_ACC_EMPTY + ab));
     }
+    if (out.leader) bulk_wait_group<0>();      // stores done before shared memory goes away
   }
 
   tc_fence_before();
@@ -382,7 +412,7 @@ static int make_map(CUtensorMap* m, const void* base, int rows, int K, int64_t l
 // M x (tiles_n tiles) output; B has b_rows rows, read per tile as two 128-row boxes (see Shape).
 template <typename Epi>
 static int launch(const void* a, int64_t lda, const void* b, int64_t ldb, int b_rows, int M, int tiles_n, int K,
-                  int b0, int b1, int b_step, const Epi& epi, cudaStream_t st) {
+                  int b0, int b1, int b_step, void* c, int64_t ldc, int c_cols, const Epi& epi, cudaStream_t st) {
   int rc = get_encode();
   if (rc) return rc;
   ENGPT_REQUIRE(aligned(a, 16) && aligned(b, 16) && (lda * 2) % 16 == 0 && (ldb * 2) % 16 == 0 && K % 8 == 0,
@@ -390,6 +420,9 @@ static int launch(const void* a, int64_t lda, const void* b, int64_t ldb, int b_
   CUtensorMap ma, mb;
   if ((rc = make_map(&ma, a, M, K, lda, BM))) return rc;
   if ((rc = make_map(&mb, b, b_rows, K, ldb, BN / 2))) return rc;
+  ENGPT_REQUIRE(aligned(c, 16) && (ldc * 2) % 16 == 0, ENGPT_ERR_ALIGN, "gemm: output needs 16-byte aligned rows");
+  CUtensorMap mc;
+  if ((rc = make_map(&mc, c, M, c_cols, ldc, BM))) return rc;   // output boxes: 64 columns x 128 rows
   Shape sh;
   sh.M = M;
   sh.N = tiles_n * BN;
@@ -405,7 +438,7 @@ static int launch(const void* a, int64_t lda, const void* b, int64_t ldb, int b_
   auto kern = gemm_kernel<Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::kDynSmem);
   if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "gemm: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid, kThreads, Layout::kDynSmem, st>>>(ma, mb, sh, epi);
+  kern<<<grid, kThreads, Layout::kDynSmem, st>>>(ma, mb, mc, sh, epi);
   return check_launch("gemm (tcgen05)");
 }
 
@@ -421,10 +454,9 @@ extern "C" int engpt_gemm_bf16(const void* a, int64_t lda, const void* b, int64_
   if ((int64_t)M * N == 0) return ENGPT_OK;
   ENGPT_REQUIRE(a && b && c, ENGPT_ERR_ARG, "gemm: null pointer");
   ENGPT_REQUIRE(lda >= K && ldb >= K && ldc >= N, ENGPT_ERR_SHAPE, "gemm: leading dimensions");
-  ENGPT_REQUIRE(aligned(c, 16) && (ldc * 2) % 16 == 0, ENGPT_ERR_ALIGN, "gemm: C needs 16-byte aligned rows");
-  gemm::StoreBf16 epi{reinterpret_cast<__nv_bfloat16*>(c), ldc, M, N};
-  return gemm::launch(a, lda, b, ldb, N, M, (N + gemm::BN - 1) / gemm::BN, K, 0, gemm::BN / 2, gemm::BN, epi,
-                      as_stream(stream));
+  gemm::StoreBf16 epi;
+  return gemm::launch(a, lda, b, ldb, N, M, (N + gemm::BN - 1) / gemm::BN, K, 0, gemm::BN / 2, gemm::BN, c, ldc, N,
+                      epi, as_stream(stream));
 }
 
 extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const float* rho, const float* cos_tab,
@@ -442,10 +474,9 @@ extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const floa
   ENGPT_REQUIRE(x && w_qkv && rho && qk_scale && qkv_out && (rope_half == 0 || (cos_tab && sin_tab)), ENGPT_ERR_ARG,
                 "qkv_projection: null pointer");
   ENGPT_REQUIRE(aligned(qkv_out, 16), ENGPT_ERR_ALIGN, "qkv_projection: output not 16-byte aligned");
-  gemm::QkvEpi epi{reinterpret_cast<__nv_bfloat16*>(qkv_out), rho, cos_tab, sin_tab, qk_scale, qk_mult, norm_eps,
-                   (int)M, T, d, rope_half};
-  return gemm::launch(x, d, w_qkv, d, 3 * d, (int)M, 3 * d / gemm::BN, d, 0, gemm::BN / 2, gemm::BN, epi,
-                      as_stream(stream));
+  gemm::QkvEpi epi{rho, cos_tab, sin_tab, qk_scale, qk_mult, norm_eps, (int)M, T, d, rope_half};
+  return gemm::launch(x, d, w_qkv, d, 3 * d, (int)M, 3 * d / gemm::BN, d, 0, gemm::BN / 2, gemm::BN, qkv_out, 3 * d,
+                      3 * d, epi, as_stream(stream));
 }
 
 extern "C" int engpt_up_gate_swiglu(const void* x, const void* w_ug, const float* s_u, const float* s_gate,
@@ -460,6 +491,7 @@ extern "C" int engpt_up_gate_swiglu(const void* x, const void* w_ug, const float
   ENGPT_REQUIRE(rows <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "up_gate_swiglu: too many rows");
   ENGPT_REQUIRE(x && w_ug && s_u && s_gate && hidden, ENGPT_ERR_ARG, "up_gate_swiglu: null pointer");
   ENGPT_REQUIRE(aligned(hidden, 16), ENGPT_ERR_ALIGN, "up_gate_swiglu: output not 16-byte aligned");
-  gemm::SwiGluEpi epi{reinterpret_cast<__nv_bfloat16*>(hidden), s_u, s_gate, u_mult, gate_mult, (int)rows, width};
-  return gemm::launch(x, d, w_ug, d, 2 * width, (int)rows, width / 128, d, 0, width, 128, epi, as_stream(stream));
+  gemm::SwiGluEpi epi{s_u, s_gate, u_mult, gate_mult};
+  return gemm::launch(x, d, w_ug, d, 2 * width, (int)rows, width / 128, d, 0, width, 128, hidden, width, width, epi,
+                      as_stream(stream));
 }
