@@ -49,6 +49,8 @@ SIGNATURES = {
     "engpt_gemm_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _i, _i, _i, _p]),
     "engpt_qkv_projection": (_i, [_p, _p, _p, _p, _p, _i, _p, _f, _f, _i, _i, _i, _i, _p, _p]),
     "engpt_up_gate_swiglu": (_i, [_p, _p, _p, _p, _f, _f, _i64, _i, _i, _p, _p]),
+    "engpt_gemm_carried_residual": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _f, _i, _f, _f, _f, _i64, _i, _p, _p,
+                                         _p, _i, _p]),
     "engpt_cross_entropy": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _p]),
     "engpt_cross_entropy_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
 }

@@ -14,6 +14,7 @@
 // in the same pass.  Bytes per row: 4d (Y) + 2d or 4d (branch) + 4d (Y') +
 // 8 (rho in/out) + aux (2d for a bf16 operand).
 #include "common.cuh"
+#include "carried_residual.cuh"
 
 namespace engpt {
 
@@ -39,40 +40,9 @@ __device__ __forceinline__ float eff_alpha(const ResidualArgs& a, float raw) {
   return (a.alpha_abs ? fabsf(raw) : raw) * a.alpha_mult;
 }
 
-struct RowScalars {
-  float coef_y;   // c_b (gauge folded in at write time)
-  float coef_b;   // rho
-  float g;        // gauge divisor (1 when inactive)
-  float inv_g;    // 1 / g
-  float rho_new;
-  float inv_rho;  // 1 / rho_new, for the Y/rho side output
-};
-
 __device__ __forceinline__ RowScalars finish_row(const ResidualArgs& a, float rho, float r0, float r1, float r2,
                                                  float r3) {
-  float cb = sqrtf(fmaxf(r0, 0.0f));
-  if (a.branch_eps > 0.f) cb = fmaxf(cb, a.branch_eps);
-  float rho_cb = rho * cb;
-  float u2 = cb * cb * r1 + rho * rho * r2 + 2.0f * rho_cb * r3;
-  float rho_plus = sqrtf(fmaxf(u2, 0.0f));
-  if (a.residual_eps > 0.f) rho_plus = fmaxf(rho_plus, a.residual_eps * rho_cb);
-  float g = 1.0f;
-  if (a.max_radius > 0.f) g = fmaxf(rho_plus / a.max_radius, 1.0f);
-  RowScalars s;
-  s.coef_y = cb;
-  s.coef_b = rho;
-  s.g = g;
-  s.inv_g = 1.0f / g;
-  s.rho_new = (g == 1.0f) ? rho_plus : rho_plus / g;
-  s.inv_rho = 1.0f / s.rho_new;
-  return s;
-}
-
-// u / g, with the per-row reciprocal (exact when the gauge is inactive, within 1 ulp otherwise)
-__device__ __forceinline__ float out_value(float alpha, float y, float b, const RowScalars& s) {
-  float beta = 1.0f - alpha;
-  float u = beta * s.coef_y * y + alpha * s.coef_b * b;
-  return u * s.inv_g;
+  return residual_row_scalars(a.branch_eps, a.residual_eps, a.max_radius, rho, r0, r1, r2, r3);
 }
 
 // Vector path: d % 8 == 0, d <= 256 * MAXCH.  Lane owns 8-column chunks

@@ -188,6 +188,10 @@ class EfficientNGPT(nn.Module):
         # bf16 mode, head_dim 64: QKV projection and its post-process in one tcgen05 GEMM (False: cuBLAS +
         # the QKV epilogue kernel in place)
         self.fuse_qkv = True
+        # bf16 mode, d in {256, 512, 768, 1024}: out_proj / down_proj GEMMs with the carried residual in
+        # their epilogue (engpt_gemm_carried_residual).  Off by default: at d=1024, T=2048, B=32 it measures
+        # slower than cuBLAS + the carried-residual kernel (0.29 vs 0.23 ms out_proj, 0.58 vs 0.48 ms down)
+        self.fuse_residual = False
         # False: logits are a strided [B, T, V] view of a [N, V rounded up to 64] buffer (no copy);
         # True: a contiguous copy is returned
         self.contiguous_logits = False
@@ -359,11 +363,22 @@ class EfficientNGPT(nn.Module):
                           self.attn_impl, st)
                 if self.attn_timer is not None:
                     self.attn_timer("stop")
-                torch.mm(ws.attn, wo.t(), out=ws.branch)
-                _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(), ws.branch.data_ptr(),
-                          act, blk.alpha_attn_raw.data_ptr(), float(blk.alpha_mult), 1, float(cfg.norm_eps),
-                          float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(),
-                          ws.rho.data_ptr(), ws.x.data_ptr(), _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H, st)
+                fuse_res = bf16 and self.fuse_residual and d % 256 == 0 and d <= 1024
+                if fuse_res:
+                    # out_proj GEMM with the carried residual in its epilogue (tcgen05, d/256-CTA clusters):
+                    # the branch never leaves the chip
+                    _lib.call("engpt_gemm_carried_residual", ws.attn.data_ptr(), d, wo.data_ptr(), d, d,
+                              ws.y.data_ptr(), ws.rho.data_ptr(), blk.alpha_attn_raw.data_ptr(),
+                              float(blk.alpha_mult), 1, float(cfg.norm_eps), float(cfg.norm_eps),
+                              float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(), ws.rho.data_ptr(),
+                              ws.x.data_ptr(), _lib.AUX_BF16_H, st)
+                else:
+                    torch.mm(ws.attn, wo.t(), out=ws.branch)
+                    _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(),
+                              ws.branch.data_ptr(), act, blk.alpha_attn_raw.data_ptr(), float(blk.alpha_mult), 1,
+                              float(cfg.norm_eps), float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d,
+                              ws.y.data_ptr(), ws.rho.data_ptr(), ws.x.data_ptr(),
+                              _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H, st)
                 if ws.ug is None:
                     # up/gate GEMM with the SwiGLU epilogue fused (tcgen05): the [n, 2W] projection never
                     # leaves TMEM
@@ -374,15 +389,23 @@ class EfficientNGPT(nn.Module):
                     torch.mm(ws.x, wug.t(), out=ws.ug)
                     _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, blk.s_u.data_ptr(), blk.s_gate.data_ptr(),
                               float(u_mult), float(sqrt_d), n, W, ws.hidden.data_ptr(), act, st)
-                torch.mm(ws.hidden, wd.t(), out=ws.branch)
                 if i < last:
                     aux_mode = _lib.AUX_BF16_Y if bf16 else _lib.AUX_NONE
                 else:
                     aux_mode = _lib.AUX_BF16_H if bf16 else _lib.AUX_F32_H
-                _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(), ws.branch.data_ptr(),
-                          act, blk.alpha_mlp_raw.data_ptr(), float(blk.alpha_mult), 1, float(cfg.norm_eps),
-                          float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(),
-                          ws.rho.data_ptr(), ws.x.data_ptr() if aux_mode != _lib.AUX_NONE else None, aux_mode, st)
+                if fuse_res and W % 8 == 0:
+                    _lib.call("engpt_gemm_carried_residual", ws.hidden.data_ptr(), W, wd.data_ptr(), W, W,
+                              ws.y.data_ptr(), ws.rho.data_ptr(), blk.alpha_mlp_raw.data_ptr(),
+                              float(blk.alpha_mult), 1, float(cfg.norm_eps), float(cfg.norm_eps),
+                              float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(), ws.rho.data_ptr(),
+                              ws.x.data_ptr(), aux_mode, st)
+                else:
+                    torch.mm(ws.hidden, wd.t(), out=ws.branch)
+                    _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(),
+                              ws.branch.data_ptr(), act, blk.alpha_mlp_raw.data_ptr(), float(blk.alpha_mult), 1,
+                              float(cfg.norm_eps), float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d,
+                              ws.y.data_ptr(), ws.rho.data_ptr(),
+                              ws.x.data_ptr() if aux_mode != _lib.AUX_NONE else None, aux_mode, st)
                 if layer_callback is not None:
                     layer_callback(i, ws.y.view(bsz, seq_len, d), ws.rho.view(bsz, seq_len))
             # output head (engpt/kernels.py:209-229 with logit_scale, engpt/models.py:366-368)

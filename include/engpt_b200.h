@@ -201,6 +201,24 @@ ENGPT_API int engpt_up_gate_swiglu(const void* x, const void* w_ug, const float*
                                    void* stream);
 
 /*
+ * Output projection with the carried residual fused into the GEMM epilogue --
+ * branch = self.out_proj(attn) / self.down_proj(hidden) (engpt/models.py:152,
+ * 172 under bf16 autocast) followed by carried_residual_gauge
+ * (engpt/kernels.py:277-324, call sites engpt/models.py:153-161, 173-181):
+ * a [rows, K] bf16 (row stride lda), w [d, K] bf16 (row stride ldw); the
+ * branch is rounded to bf16 as the autocast GEMM output is and never stored.
+ * y, rho, alpha, the epsilons, y_out, rho_out, aux_out and aux_mode
+ * (ENGPT_AUX_NONE, _BF16_Y or _BF16_H) mean what they mean for
+ * engpt_carried_residual_gauge; y_out may be y and rho_out may be rho.
+ * d in {256, 512, 768, 1024}; K a multiple of 8.
+ */
+ENGPT_API int engpt_gemm_carried_residual(const void* a, int64_t lda, const void* w, int64_t ldw, int K,
+                                          const float* y, const float* rho, const float* alpha, float alpha_mult,
+                                          int alpha_abs, float branch_eps, float residual_eps, float max_radius,
+                                          int64_t rows, int d, float* y_out, float* rho_out, void* aux_out,
+                                          int aux_mode, void* stream);
+
+/*
  * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).
  * logits [rows, vocab] with leading dimension ld (elements), `dtype`;
  * targets int64 [rows].  row_loss [rows] fp32 is caller-provided scratch;

@@ -356,3 +356,77 @@ def test_qkv_projection_matches_unfused_path(cuda, B, T):
               Dh // 2, qks.data_ptr(), 2.0, 1e-6, B, T, H, Dh, None, None, None, _lib.QKV_INPLACE, _stream())
     diff = (fused.float() - unf.float()).abs().max().item()
     assert diff <= 2e-2 * unf.float().abs().max().item(), diff
+
+
+def _residual_case(cuda, rows, d, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randn(rows, K, generator=g) * 0.5).to(cuda, torch.bfloat16)
+    w = (torch.randn(d, K, generator=g) / K ** 0.5).to(cuda, torch.bfloat16)
+    y = torch.randn(rows, d, generator=g).to(cuda)
+    rho = (torch.rand(rows, generator=g) * 3 + 0.25).to(cuda)
+    alpha = (torch.rand(d, generator=g) - 0.3).to(cuda)     # some negative: alpha_abs folds them
+    return a, w, y, rho, alpha
+
+
+@pytest.mark.parametrize("rows,d,K,aux_mode", [(200, 256, 256, 2), (1000, 512, 1024, 1), (300, 1024, 1024, 2),
+                                               (4224, 1024, 4096, 1), (129, 768, 512, 0)])
+def test_gemm_carried_residual_matches_unfused_path(cuda, rows, d, K, aux_mode):
+    """GEMM + carried residual in one kernel (clusters of d/256 CTAs) vs the GEMM, then engpt_carried_residual_gauge
+    (engpt/kernels.py:277-324) on its bf16 output."""
+    a, w, y, rho, alpha = _residual_case(cuda, rows, d, K, rows + d)
+    branch = torch.mm(a, w.t())
+    # max radius = the median ungauged rho+, so the gauge is active on about half of the rows
+    y0, r0 = torch.empty_like(y), torch.empty_like(rho)
+    _lib.call("engpt_carried_residual_gauge", y.data_ptr(), rho.data_ptr(), branch.data_ptr(), _lib.BF16,
+              alpha.data_ptr(), 0.7, 1, 1e-6, 1e-6, 0.0, rows, d, y0.data_ptr(), r0.data_ptr(), None, 0, _stream())
+    max_radius = r0.median().item()
+    args = (alpha.data_ptr(), 0.7, 1, 1e-6, 1e-6, max_radius, rows, d)
+    yo = torch.empty_like(y)
+    ro = torch.empty_like(rho)
+    aux = torch.empty(rows, d, device=cuda, dtype=torch.bfloat16)
+    _lib.call("engpt_gemm_carried_residual", a.data_ptr(), K, w.data_ptr(), K, K, y.data_ptr(), rho.data_ptr(), *args,
+              yo.data_ptr(), ro.data_ptr(), aux.data_ptr() if aux_mode else None, aux_mode, _stream())
+    yr, rr = torch.empty_like(y), torch.empty_like(rho)
+    auxr = torch.empty_like(aux)
+    _lib.call("engpt_carried_residual_gauge", y.data_ptr(), rho.data_ptr(), branch.data_ptr(), _lib.BF16, *args,
+              yr.data_ptr(), rr.data_ptr(), auxr.data_ptr() if aux_mode else None, aux_mode, _stream())
+    torch.cuda.synchronize()
+    gauged = (r0 > max_radius).sum().item()
+    assert 0 < gauged < rows                        # both gauge branches are exercised
+    # the two GEMMs may round a branch element to neighbouring bf16 values: compare at bf16 resolution
+    assert ((yo - yr).abs().max() / yr.abs().max()).item() < 1e-2
+    assert ((ro - rr).abs() / rr).max().item() < 1e-2
+    assert ((yo / ro[:, None]) - (yr / rr[:, None])).abs().max().item() < 2e-2
+    if aux_mode:
+        assert ((aux.float() - auxr.float()).abs().max() / auxr.float().abs().max()).item() < 2e-2
+
+
+def test_gemm_carried_residual_in_place_is_exact(cuda):
+    """y_out = y and rho_out = rho (how the forward calls it) give bit-identical results to separate outputs."""
+    rows, d, K = 777, 1024, 1024
+    a, w, y, rho, alpha = _residual_case(cuda, rows, d, K, 5)
+    args = (alpha.data_ptr(), 1.0, 1, 1e-6, 1e-6, 4.0, rows, d)
+    yo, ro = torch.empty_like(y), torch.empty_like(rho)
+    aux1 = torch.empty(rows, d, device=cuda, dtype=torch.bfloat16)
+    aux2 = torch.empty_like(aux1)
+    _lib.call("engpt_gemm_carried_residual", a.data_ptr(), K, w.data_ptr(), K, K, y.data_ptr(), rho.data_ptr(), *args,
+              yo.data_ptr(), ro.data_ptr(), aux1.data_ptr(), _lib.AUX_BF16_H, _stream())
+    yi, ri = y.clone(), rho.clone()
+    _lib.call("engpt_gemm_carried_residual", a.data_ptr(), K, w.data_ptr(), K, K, yi.data_ptr(), ri.data_ptr(),
+              *args, yi.data_ptr(), ri.data_ptr(), aux2.data_ptr(), _lib.AUX_BF16_H, _stream())
+    torch.cuda.synchronize()
+    assert torch.equal(yo, yi) and torch.equal(ro, ri) and torch.equal(aux1, aux2)
+
+
+def test_gemm_carried_residual_rejects_unsupported(cuda):
+    """d = 1280 would need a cluster of 5 CTAs: refused with ENGPT_ERR_UNSUPPORTED before any device work."""
+    a = torch.zeros(128, 256, device=cuda, dtype=torch.bfloat16)
+    w = torch.zeros(1280, 256, device=cuda, dtype=torch.bfloat16)
+    y = torch.zeros(128, 1280, device=cuda)
+    rho = torch.ones(128, device=cuda)
+    alpha = torch.zeros(1280, device=cuda)
+    with pytest.raises(_lib.EngptError) as ei:
+        _lib.call("engpt_gemm_carried_residual", a.data_ptr(), 256, w.data_ptr(), 256, 256, y.data_ptr(),
+                  rho.data_ptr(), alpha.data_ptr(), 1.0, 1, 1e-6, 1e-6, 0.0, 128, 1280, y.data_ptr(), rho.data_ptr(),
+                  None, 0, _stream())
+    assert ei.value.code == 6   # ENGPT_ERR_UNSUPPORTED

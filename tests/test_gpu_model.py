@@ -49,9 +49,10 @@ def test_small_model_fp32_matches_reference(golden, cuda):
         assert row_rel_err(h, g[f"y{i}"] / g[f"rho{i}"][..., None]) < FP32_TOL
 
 
-def _cfg_run(golden, cuda, name, cfg, bf16, batch_rows=None):
+def _cfg_run(golden, cuda, name, cfg, bf16, batch_rows=None, fuse_residual=False):
     g = golden(name)
     model = seeded_model(cfg, seed=0).to(cuda)
+    model.fuse_residual = fuse_residual
     idx = torch.as_tensor(g["idx"].astype(np.int64))
     tgt = torch.as_tensor(g["targets"].astype(np.int64))
     if batch_rows is not None:
@@ -89,9 +90,12 @@ def test_cfg1_bf16_matches_reference(golden, cuda):
     assert abs(loss.item() - float(g["loss"])) < LOSS_TOL
 
 
-def test_cfg4_deep_stack_bf16_gauge(golden, cuda):
-    """128 layers, gauge active from layer ~8: Y and rho stay finite and Y/rho tracks the reference."""
-    g, _, logits, loss, states = _cfg_run(golden, cuda, "cfg4_deep.npz", CFG4, bf16=True)
+@pytest.mark.parametrize("fuse_residual", [False, True])
+def test_cfg4_deep_stack_bf16_gauge(golden, cuda, fuse_residual):
+    """128 layers, gauge active from layer ~8: Y and rho stay finite and Y/rho tracks the reference (with the
+    carried residual in its own kernel, and fused into the out_proj / down_proj GEMM epilogues)."""
+    g, _, logits, loss, states = _cfg_run(golden, cuda, "cfg4_deep.npz", CFG4, bf16=True,
+                                          fuse_residual=fuse_residual)
     worst = _check_states(g, states, BF16_TOL)
     rho_max = max(float(r.max()) for _, r in states)
     assert rho_max == pytest.approx(1024.0, rel=1e-5)  # the gauge engaged
@@ -165,3 +169,23 @@ def test_block_module_call_matches_engine(cuda):
     h_engine = (states[-1][0] / states[-1][1].unsqueeze(-1)).cpu().numpy()
     h_block = (y / rho.unsqueeze(-1)).float().cpu().numpy()
     assert row_rel_err(h_block.reshape(-1, 128), h_engine.reshape(-1, 128)) < 1e-2
+
+
+@pytest.mark.parametrize("d,H", [(1024, 16), (512, 8)])
+def test_fused_residual_gemm_matches_unfused_forward(cuda, d, H):
+    """bf16 forward with the out_proj / down_proj GEMMs carrying the residual in their epilogue (clusters of
+    d/256 CTAs) vs cuBLAS + the standalone carried-residual kernel: Y/rho per layer and the loss."""
+    cfg = dict(vocab_size=1000, block_size=256, n_layer=3, n_head=H, n_embd=d, mlp_ratio=4.0, dropout=0.0)
+    model = seeded_model(cfg, seed=11).to(cuda)
+    gen = torch.Generator().manual_seed(2)
+    idx = torch.randint(0, 1000, (3, 256), generator=gen).to(cuda)
+    tgt = torch.randint(0, 1000, (3, 256), generator=gen).to(cuda)
+    model.fuse_residual = True
+    _, loss_f, st_f = _run(model, idx, tgt, bf16=True)
+    model.fuse_residual = False
+    _, loss_u, st_u = _run(model, idx, tgt, bf16=True)
+    for (yf, rf), (yu, ru) in zip(st_f, st_u):
+        hf = (yf / rf.unsqueeze(-1)).reshape(-1, d).cpu().numpy()
+        hu = (yu / ru.unsqueeze(-1)).reshape(-1, d).cpu().numpy()
+        assert row_rel_err(hf, hu) < BF16_TOL
+    assert abs(loss_f.item() - loss_u.item()) < LOSS_TOL
