@@ -409,6 +409,7 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
     flops = {   # tensor-bound fused GEMMs: 2 * M * N * K
         "engpt_qkv_projection": 2.0 * n * 3 * d * d,
         "engpt_up_gate_swiglu": 2.0 * n * 2 * W * d,
+        "engpt_logits_cross_entropy": 2.0 * n * a.vocab * d,         # output head (+ log-sum-exp epilogue)
     }
     out = {}
     for name, evs in per.items():

@@ -52,6 +52,7 @@ SIGNATURES = {
     "engpt_gemm_carried_residual": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _f, _i, _f, _f, _f, _i64, _i, _p, _p,
                                          _p, _i, _p]),
     "engpt_cross_entropy": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "engpt_logits_cross_entropy": (_i, [_p, _p, _i64, _i, _i64, _p, _i64, _p, _p, _p, _p, _p]),
     "engpt_cross_entropy_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
 }
 CE_NOALLOC_MAX_ROWS = 262144

@@ -359,6 +359,11 @@ __global__ void __launch_bounds__(1024) mean_loss_kernel(const float* __restrict
   if (threadIdx.x == 0) out[0] = scnt[0] > 0 ? (float)(sacc[0] / (double)scnt[0]) : NAN;
 }
 
+int launch_mean_loss(const float* row_loss, const int64_t* targets, int64_t rows, float* loss_out, cudaStream_t st) {
+  mean_loss_kernel<<<1, 1024, 0, st>>>(row_loss, targets, rows, loss_out);
+  return check_launch("cross_entropy_mean");
+}
+
 static int grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   int64_t cap = (int64_t)num_sms() * 16;

@@ -15,6 +15,8 @@ namespace engpt {
 int set_error(int code, const char* fmt, ...);
 void clear_error();
 int check_launch(const char* what);
+// Mean of row_loss over the rows whose target is not -100 (F.cross_entropy's reduction) into loss_out[0].
+int launch_mean_loss(const float* row_loss, const int64_t* targets, int64_t rows, float* loss_out, cudaStream_t st);
 
 #define ENGPT_REQUIRE(cond, code, ...)            \
   do {                                            \

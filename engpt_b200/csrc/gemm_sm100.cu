@@ -4,8 +4,9 @@
 // The dense projections of the enGPT block (engpt/models.py:140-182) are this
 // shape with A = the activations and B = an nn.Linear weight.  A CTA owns one
 // SM and walks 128 x 256 output tiles (tile t = blockIdx.x + i * gridDim.x,
-// row-block major, so the 256 KB A row-block a wave of CTAs shares stays in
-// L2).  Warp roles (192 threads):
+// in groups of 8 row blocks with the tile columns outer inside a group, so
+// the A row blocks and the band of B a wave of CTAs shares stay in L2).
+// Warp roles (192 threads):
 //   warp 0      TMA producer: 64-wide K slices of A (128 rows) and B (256 rows)
 //               into a 4-stage shared-memory ring (128-byte swizzle)
 //   warp 1      TMEM allocator + MMA issuer (the whole warp runs the loop; one
@@ -64,6 +65,20 @@ struct Shape {
   // (accumulator columns 0-127 and 128-255).  Plain GEMM: b0 = 0, b1 = 128, b_step = 256.  Up/gate with
   // SwiGLU: b0 = 0, b1 = width (the gate half of the weight), b_step = 128.
   int b0, b1, b_step;
+  int row_blocks;       // ceil(M / BM)
+  int group;            // row blocks per raster group (tile order below)
+  // Tile t -> (row block, tile column): groups of `group` row blocks, tile columns outer inside a group, so
+  // the tiles in flight at once share a few row blocks of A and a narrow band of B columns (a large B, such
+  // as the 50k-row output head, then stays in L2 while the group's row blocks reuse it).
+  __device__ __forceinline__ void coords(int t, int& m0, int& tn) const {
+    const int per_group = group * tiles_n;
+    const int g = t / per_group;
+    const int rem = t - g * per_group;
+    const int rb0 = g * group;
+    const int gs = min(group, row_blocks - rb0);
+    tn = rem / gs;
+    m0 = (rb0 + rem - tn * gs) * BM;
+  }
 };
 
 // Output staging: each epilogue thread writes its row's 64 bf16 results of one output chunk (128 bytes)
@@ -249,6 +264,57 @@ struct SwiGluEpi {
   }
 };
 
+// Output head + the log-sum-exp half of F.cross_entropy (engpt/models.py:328-333): the bf16 logits tile is
+// stored as by StoreBf16, and from the same bf16-rounded values (what the loss reads under autocast) each row's
+// base-2 log-sum-exp over the tile's valid columns (< vocab) is written as a (max, sum) pair to
+// part[tn * rows + m].  The pairs of a row merge into its full log-sum-exp in ce_combine_kernel.
+struct LseEpi {
+  float2* part;
+  int rows;
+  int vocab;
+  __device__ __forceinline__ void tile(int m0, int m, int tn, uint32_t tacc, OutStage& out) const {
+    constexpr float kL2e = 1.4426950408889634f;
+    const int nvalid = vocab - tn * BN;          // valid columns of this tile (>= 1)
+    float mx = -INFINITY, sm = 0.f;              // base-2 running max and sum
+#pragma unroll 1
+    for (int oc = 0; oc < BN / 64; ++oc) {
+      float v[64];
+      load_acc32(tacc + 64 * oc, v);
+      load_acc32(tacc + 64 * oc + 32, v + 32);
+      uint4 o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o[j] = pack8(v + 8 * j);
+        unpack8(o[j], v + 8 * j);               // the stored (rounded) logits
+      }
+      out.put(tn * BN + 64 * oc, m0, o);
+      if (nvalid < BN) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (64 * oc + i >= nvalid) v[i] = -INFINITY;
+      }
+      float cm = v[0];
+#pragma unroll
+      for (int i = 1; i < 64; ++i) cm = fmaxf(cm, v[i]);
+      if (cm == -INFINITY) continue;             // every column of this chunk is past the vocab
+      const float cml = cm * kL2e;
+      if (cml > mx) {
+        sm *= ex2_approx(mx - cml);
+        mx = cml;
+      }
+      const float nm = -mx;
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        s0 += ex2_approx(fmaf(v[i], kL2e, nm));
+        s1 += ex2_approx(fmaf(v[i + 1], kL2e, nm));
+      }
+      sm += s0 + s1;
+    }
+    if (m < rows) part[(int64_t)tn * rows + m] = make_float2(mx, sm);
+  }
+};
+
 template <typename Epi>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -296,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int i = 0; ok && i < my_tiles; ++i) {
         const int t = blockIdx.x + i * gridDim.x;
-        const int m0 = (t / sh.tiles_n) * BM;
-        const int tn = t % sh.tiles_n;
+        int m0, tn;
+        sh.coords(t, m0, tn);
         const int nb0 = sh.b0 + tn * sh.b_step;
         const int nb1 = sh.b1 + tn * sh.b_step;
         for (int kb = 0; kb < kb_n; ++kb, ++it) {
@@ -362,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < my_tiles; ++i) {
       const int ab = i & 1;
       const int t = blockIdx.x + i * gridDim.x;
-      const int m0 = (t / sh.tiles_n) * BM;
-      const int tn = t % sh.tiles_n;
+      int m0, tn;
+      sh.coords(t, m0, tn);
       const bool ok = mbar_wait(bar(B_ACC_FULL + ab), (i >> 1) & 1, abort_flag, 54);
       if (bar_red_or(1, 128, !ok)) break;     // the four epilogue warps leave together
       tc_fence_after();
@@ -845,7 +911,9 @@ static int launch(const void* a, int64_t lda, const void* b, int64_t ldb, int b_
   sh.b0 = b0;
   sh.b1 = b1;
   sh.b_step = b_step;
-  const int64_t tiles = (int64_t)((M + BM - 1) / BM) * sh.tiles_n;
+  sh.row_blocks = (M + BM - 1) / BM;
+  sh.group = 8;
+  const int64_t tiles = (int64_t)sh.row_blocks * sh.tiles_n;
   ENGPT_REQUIRE(tiles <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "gemm: too many tiles");
   sh.tiles = (int)tiles;
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
@@ -1045,4 +1113,65 @@ extern "C" int engpt_gemm_carried_residual(const void* a, int64_t lda, const voi
   e = cudaLaunchKernelEx(&cfg, kern, ma, mb, my, myo, max_, p);
   if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "gemm_carried_residual: launch: %s", cudaGetErrorString(e));
   return check_launch("gemm_carried_residual (tcgen05)");
+}
+
+namespace engpt {
+namespace gemm {
+
+// Row r: merge the (max, sum) pairs of its tiles into log-sum-exp, minus the stored bf16 logit of the target
+// (ignore_index -100 rows give 0, as F.cross_entropy does).
+__global__ void __launch_bounds__(256) ce_combine_kernel(const float2* __restrict__ part, int tiles, int rows,
+                                                         const __nv_bfloat16* __restrict__ logits, int64_t ld,
+                                                         int64_t vocab, const int64_t* __restrict__ targets,
+                                                         float* __restrict__ row_loss) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float M = -INFINITY, S = 0.f;
+  for (int t = 0; t < tiles; ++t) {
+    const float2 q = part[(int64_t)t * rows + r];
+    const float mm = fmaxf(M, q.x);
+    if (mm == -INFINITY) continue;
+    S = S * ex2_approx(M - mm) + q.y * ex2_approx(q.x - mm);
+    M = mm;
+  }
+  const int64_t t = targets[r];
+  float loss;
+  if (t == -100) {
+    loss = 0.f;
+  } else if (t < 0 || t >= vocab) {
+    record_device_error(ENGPT_ERR_ARG, 3);
+    loss = NAN;
+  } else {
+    loss = (M + log2f(S)) * 0.6931471805599453f - __bfloat162float(logits[(int64_t)r * ld + t]);
+  }
+  row_loss[r] = loss;
+}
+
+}  // namespace gemm
+}  // namespace engpt
+
+extern "C" int engpt_logits_cross_entropy(const void* x, const void* w_head, int64_t rows, int d, int64_t vocab,
+                                          void* logits, int64_t ld, const int64_t* targets, void* partials,
+                                          float* row_loss, float* loss_out, void* stream) {
+  using namespace gemm;
+  clear_error();
+  ENGPT_REQUIRE(rows > 0 && d > 0 && vocab > 0 && ld >= vocab, ENGPT_ERR_SHAPE,
+                "logits_cross_entropy: rows=%lld d=%d vocab=%lld ld=%lld", (long long)rows, d, (long long)vocab,
+                (long long)ld);
+  ENGPT_REQUIRE(rows <= 0x7fffffffLL && vocab <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "logits_cross_entropy: too large");
+  ENGPT_REQUIRE(x && w_head && logits && targets && partials && row_loss && loss_out, ENGPT_ERR_ARG,
+                "logits_cross_entropy: null pointer");
+  ENGPT_REQUIRE(d % 8 == 0 && ld % 8 == 0 && aligned(logits, 16) && aligned(partials, 8), ENGPT_ERR_ALIGN,
+                "logits_cross_entropy: d and ld must be multiples of 8, logits 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const int tiles_n = (int)((vocab + BN - 1) / BN);
+  LseEpi epi{reinterpret_cast<float2*>(partials), (int)rows, (int)vocab};
+  int rc = launch(x, d, w_head, d, (int)vocab, (int)rows, tiles_n, d, 0, BN / 2, BN, logits, ld, (int)vocab, epi, st);
+  if (rc) return rc;
+  ce_combine_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const float2*>(partials), tiles_n, (int)rows, reinterpret_cast<const __nv_bfloat16*>(logits),
+      ld, vocab, targets, row_loss);
+  rc = check_launch("ce_combine");
+  if (rc) return rc;
+  return launch_mean_loss(row_loss, targets, rows, loss_out, st);
 }

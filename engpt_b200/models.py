@@ -163,6 +163,15 @@ class _Workspace:
         # sends cuBLAS to a ~10x slower kernel
         self.vocab_pad = -(-cfg.vocab_size // 64) * 64
         self.w_head = torch.zeros(self.vocab_pad, d, device=device, dtype=act)
+        self._lse = None
+        self._lse_shape = (-(-cfg.vocab_size // 256) * n * 2,)
+        self._device = device
+
+    def lse_partials(self) -> torch.Tensor:
+        """Scratch of the fused head: one (max, sum) pair per row and 256-column logits tile."""
+        if self._lse is None:
+            self._lse = torch.empty(self._lse_shape, device=self._device, dtype=torch.float32)
+        return self._lse
 
 
 class EfficientNGPT(nn.Module):
@@ -192,6 +201,9 @@ class EfficientNGPT(nn.Module):
         # their epilogue (engpt_gemm_carried_residual).  Off by default: at d=1024, T=2048, B=32 it measures
         # slower than cuBLAS + the carried-residual kernel (0.29 vs 0.23 ms out_proj, 0.58 vs 0.48 ms down)
         self.fuse_residual = False
+        # bf16 mode with targets: output-head GEMM with the cross-entropy's log-sum-exp in its epilogue
+        # (engpt_logits_cross_entropy; False: cuBLAS logits + the cross-entropy kernel)
+        self.fuse_head = True
         # False: logits are a strided [B, T, V] view of a [N, V rounded up to 64] buffer (no copy);
         # True: a contiguous copy is returned
         self.contiguous_logits = False
@@ -415,18 +427,26 @@ class EfficientNGPT(nn.Module):
             # first V columns (row stride V_pad); values are those of the [N, V] product
             vp = ws.vocab_pad
             logits_buf = torch.empty(n, vp, device=dev, dtype=ws.act)
-            torch.mm(ws.x, ws.w_head.t(), out=logits_buf)
+            loss = None
+            if targets is not None and targets.ndim != 2:
+                raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
+            if targets is not None and bf16 and self.fuse_head and d % 8 == 0:
+                # logits GEMM (tcgen05) with the per-tile log-sum-exp in its epilogue, then the merge
+                t = targets.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
+                loss = torch.empty((), device=dev, dtype=torch.float32)
+                _lib.call("engpt_logits_cross_entropy", ws.x.data_ptr(), ws.w_head.data_ptr(), n, d, cfg.vocab_size,
+                          logits_buf.data_ptr(), vp, t.data_ptr(), ws.lse_partials().data_ptr(),
+                          ws.row_loss.data_ptr(), loss.data_ptr(), st)
+            else:
+                torch.mm(ws.x, ws.w_head.t(), out=logits_buf)
+                if targets is not None:
+                    t = targets.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
+                    loss = torch.empty((), device=dev, dtype=torch.float32)
+                    _lib.call("engpt_cross_entropy", logits_buf.data_ptr(), act, n, cfg.vocab_size, vp,
+                              t.data_ptr(), ws.row_loss.data_ptr(), loss.data_ptr(), st)
             logits = logits_buf.view(bsz, seq_len, vp)[:, :, :cfg.vocab_size]
             if self.contiguous_logits:
                 logits = logits.contiguous()
-            loss = None
-            if targets is not None:
-                if targets.ndim != 2:
-                    raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
-                t = targets.to(device=dev, dtype=torch.int64, non_blocking=True).contiguous()
-                loss = torch.empty((), device=dev, dtype=torch.float32)
-                _lib.call("engpt_cross_entropy", logits_buf.data_ptr(), act, n, cfg.vocab_size, vp,
-                          t.data_ptr(), ws.row_loss.data_ptr(), loss.data_ptr(), st)
         return logits, loss
 
     def forward_with_states(self, idx: Tensor, targets: Optional[Tensor] = None):

@@ -219,6 +219,21 @@ ENGPT_API int engpt_gemm_carried_residual(const void* a, int64_t lda, const void
                                           int aux_mode, void* stream);
 
 /*
+ * Output head and token cross-entropy in one pass over the logits --
+ * F.linear(x, w_head) of engpt/kernels.py:209-229 (x = bf16(Y / rho), w_head
+ * = bf16(E_out * s_z_eff), [vocab, d]) followed by F.cross_entropy
+ * (engpt/models.py:328-333, mean, ignore_index -100).  The tcgen05 GEMM
+ * stores the bf16 logits [rows, vocab] (row stride ld) and, from the same
+ * bf16 values, each row's log-sum-exp per 256-column tile into `partials`
+ * (scratch of ceil(vocab / 256) * rows float pairs); a second kernel merges
+ * them, subtracts the target's logit into row_loss [rows] (scratch) and
+ * loss_out receives the fp32 mean.  d and ld multiples of 8.
+ */
+ENGPT_API int engpt_logits_cross_entropy(const void* x, const void* w_head, int64_t rows, int d, int64_t vocab,
+                                         void* logits, int64_t ld, const int64_t* targets, void* partials,
+                                         float* row_loss, float* loss_out, void* stream);
+
+/*
  * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).
  * logits [rows, vocab] with leading dimension ld (elements), `dtype`;
  * targets int64 [rows].  row_loss [rows] fp32 is caller-provided scratch;

@@ -430,3 +430,39 @@ def test_gemm_carried_residual_rejects_unsupported(cuda):
                   rho.data_ptr(), alpha.data_ptr(), 1.0, 1, 1e-6, 1e-6, 0.0, 128, 1280, y.data_ptr(), rho.data_ptr(),
                   None, 0, _stream())
     assert ei.value.code == 6   # ENGPT_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("rows,d,vocab,ld", [(300, 256, 1000, 1024), (256, 1024, 50257, 50304), (129, 512, 300, 304)])
+def test_logits_cross_entropy_matches_unfused_path(cuda, rows, d, vocab, ld):
+    """Head GEMM with the log-sum-exp in its epilogue + the merge kernel vs cuBLAS logits + engpt_cross_entropy and
+    F.cross_entropy on the same bf16 logits (engpt/models.py:328-333), including ignore_index rows and a vocab that
+    is not a multiple of the 256-column tile."""
+    g = torch.Generator().manual_seed(vocab)
+    x = (torch.randn(rows, d, generator=g) * 2.0).to(cuda, torch.bfloat16)
+    w = (torch.randn(vocab, d, generator=g) / d ** 0.5).to(cuda, torch.bfloat16)
+    tgt = torch.randint(0, vocab, (rows,), generator=g)
+    tgt[::7] = -100
+    tgt = tgt.to(cuda)
+    tiles = -(-vocab // 256)
+    logits = torch.full((rows, ld), float("nan"), device=cuda, dtype=torch.bfloat16)
+    part = torch.empty(tiles * rows * 2, device=cuda)
+    row_loss = torch.empty(rows, device=cuda)
+    loss = torch.empty((), device=cuda)
+    _lib.call("engpt_logits_cross_entropy", x.data_ptr(), w.data_ptr(), rows, d, vocab, logits.data_ptr(), ld,
+              tgt.data_ptr(), part.data_ptr(), row_loss.data_ptr(), loss.data_ptr(), _stream())
+    ref_logits = torch.mm(x, w.t())
+    got = logits[:, :vocab].float()
+    assert ((got - ref_logits.float()).abs().max() / ref_logits.float().abs().max()).item() < 1e-2
+    # the loss of the fused path on its own logits equals F.cross_entropy of those logits
+    ref = torch.nn.functional.cross_entropy(got, tgt, ignore_index=-100)
+    assert abs(loss.item() - ref.item()) < 1e-3, (loss.item(), ref.item())
+    valid = tgt != -100
+    rl_ref = torch.nn.functional.cross_entropy(got, tgt.clamp(min=0), reduction="none")
+    assert (row_loss[valid] - rl_ref[valid]).abs().max().item() < 2e-3
+    assert (row_loss[~valid] == 0).all()
+    # and the unfused production path (cuBLAS logits, then the cross-entropy kernel)
+    rl2 = torch.empty_like(row_loss)
+    loss2 = torch.empty((), device=cuda)
+    _lib.call("engpt_cross_entropy", ref_logits.data_ptr(), _lib.BF16, rows, vocab, vocab, tgt.data_ptr(),
+              rl2.data_ptr(), loss2.data_ptr(), _stream())
+    assert abs(loss.item() - loss2.item()) < 1e-2
