@@ -383,6 +383,7 @@ struct Layout {
   static constexpr int kDynSmem = TOTAL + 1024;
 };
 
+namespace barriers {
 enum {
   B_Q = 0,
   B_KFULL = 1,                   // + stage (NS)
@@ -395,6 +396,8 @@ enum {
   B_FINAL = B_ODONE + 4,
   B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
+}  // namespace barriers
+using namespace barriers;
 static_assert(B_PAIR + 8 <= Layout::kBars, "barrier slots");
 
 constexpr uint32_t kColO = 384;      // + 64 * tile; slots at 128 * slot
@@ -702,8 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto xslot = [&](int par, int half) -> float* { return xch + ((par * 2 + w) * 2 + half) * 128 + row; };
     const uint32_t pair = bar(B_PAIR + 4 * w + wq);
     uint32_t pair_phase = 0;
-    // the two halves of these rows swap one value through shared memory (bounded mbarrier handshake)
-    auto swap = [&](float mine, int par, bool& good) -> float {
+    // the two halves of these rows swap one value through shared memory (bounded mbarrier handshake); the
+    // exchange slot alternates with the handshake count, so a value is never overwritten before it is read
+    auto swap = [&](float mine, int, bool& good) -> float {
+      const int par = (int)(pair_phase & 1);
       *xslot(par, hf) = mine;
       mbar_arrive(pair);
       good = good && __all_sync(0xffffffffu, mbar_wait(pair, pair_phase & 1, abort_flag, 33));
@@ -715,68 +720,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     st.kr = 0.f;
     st.l2 = f2_pack(0.f, 0.f);
     bool ok = true;
+    const int pair_bar = 1 + 4 * w + wq;   // named barrier of the two warps that share these rows
     for (int j = 0; j < n_w; ++j) {
+      // A failed (timed-out) wait poisons this warp: it skips the remaining work of the band but still takes
+      // every pair barrier below, so the other warp of the pair never waits on a barrier this one skips.
       const int g = bd.job_of(w, j);
       const int slot = g % NSLOT;
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (g / NSLOT) & 1, abort_flag, 28));
-      if (!ok) break;
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (g / NSLOT) & 1, abort_flag, 28));
       // O completion barriers alternate by tile parity, and each tile first waits for the PV two tiles
       // back, so any later parity wait on them is never more than one phase behind
-      if (j >= 2) {
+      if (ok && j >= 2)
         ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + 2 * w + (j & 1)), ((j - 2) >> 1) & 1, abort_flag, 29));
-        if (!ok) break;
-      }
-      tc_fence_after();
       const uint32_t tS = tmem + 128 * slot + t_lane;
       const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
       const int kbase = j * BN + 64 * hf;    // this half's first key
-      const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
-      uint32_t r[32];
-      if (j == 0) {
-        // common reference max: the larger of the two halves' first-chunk maxima (key 0 is always visible)
-        tmem_ld32(tS + 64 * hf, r);
-        tmem_wait_ld32(r);
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (kbase + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
-        mx = fmaxf(mx, swap(mx, 1, ok));
-        st.m = mx * sl2;
-        if (!ok) break;
-      }
       st.kr = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        tmem_ld32(tS + 64 * hf + 32 * cc, r);
-        tmem_wait_ld32(r);
-        softmax_chunk(r, tP0 + 16 * cc, tP0, cc, kbase + 32 * cc, q_idx, sl2, diag, st);
-      }
-      // agree on the tile's raise with the other half of the rows
-      const float k_all = fmaxf(st.kr, swap(st.kr, j & 1, ok));
-      if (!ok) break;
-      if (__any_sync(0xffffffffu, k_all > 0.0f)) {
-        tmem_wait_st();
-        const float fp = pow2_neg(k_all - st.kr);     // this half's P and l: from m + kr to m + k_all
-        scale_cols16<true>(tP0, fp);
-        scale_cols16<true>(tP0 + 16, fp);
-        float la, lb;
-        f2_unpack(st.l2, la, lb);
-        st.l2 = f2_pack(la * fp, lb * fp);
-        if (j > 0) {
-          // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(bar(B_ODONE + 2 * w + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, 32));
-          if (!ok) break;
-          tc_fence_after();
-          const float fo = pow2_neg(k_all);
-          scale_cols16<false>(tO, fo);
-          scale_cols16<false>(tO + 16, fo);
+      if (ok) {
+        tc_fence_after();
+        const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
+        uint32_t r[32];
+        if (j == 0) {
+          // common reference max: the larger of the two halves' first-chunk maxima (key 0 is always visible)
+          tmem_ld32(tS + 64 * hf, r);
+          tmem_wait_ld32(r);
+          float mx = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (kbase + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
+          mx = fmaxf(mx, swap(mx, 1, ok));
+          st.m = mx * sl2;
         }
-        st.m += k_all;
+        if (ok) {
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            tmem_ld32(tS + 64 * hf + 32 * cc, r);
+            tmem_wait_ld32(r);
+            softmax_chunk(r, tP0 + 16 * cc, tP0, cc, kbase + 32 * cc, q_idx, sl2, diag, st);
+          }
+        }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(B_TDONE + slot));
+      // did either half of these rows raise m in this tile?  (a 64-thread barrier with an OR; the raises are
+      // exchanged through shared memory only when one did)
+      if (bar_red_or(pair_bar, 64, ok && st.kr > 0.0f) && ok) {
+        const float k_all = fmaxf(st.kr, swap(st.kr, 0, ok));
+        if (ok) {
+          tmem_wait_st();
+          const float fp = pow2_neg(k_all - st.kr);     // this half's P and l: from m + kr to m + k_all
+          scale_cols16<true>(tP0, fp);
+          scale_cols16<true>(tP0 + 16, fp);
+          float la, lb;
+          f2_unpack(st.l2, la, lb);
+          st.l2 = f2_pack(la * fp, lb * fp);
+          if (j > 0) {
+            // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(bar(B_ODONE + 2 * w + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, 32));
+            if (ok) {
+              tc_fence_after();
+              const float fo = pow2_neg(k_all);
+              scale_cols16<false>(tO, fo);
+              scale_cols16<false>(tO + 16, fo);
+            }
+          }
+          st.m += k_all;
+        }
+      }
+      if (ok) {
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(B_TDONE + slot));
+      }
     }
     if (ok && n_w > 0) {
       float la, lb;
@@ -818,6 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace v2
+
 
 // --------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
