@@ -233,7 +233,8 @@ def run_reference(a, world, rank):
 
 # ------------------------------------------------------------------ GPU arm
 # kernels launched per C-ABI call
-LAUNCHES = {"engpt_cross_entropy": 2}
+# kernels launched per C-ABI call (1 unless listed)
+LAUNCHES = {"engpt_cross_entropy": 2, "engpt_logits_cross_entropy": 3}
 
 
 def run_gpu(a, world, rank, local_rank):
