@@ -14,6 +14,8 @@
 // MMAs, frees TMEM and returns.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "sm100_ptx.cuh"
 
@@ -371,12 +373,11 @@ constexpr int kWarpTMA = 16;
 constexpr int kWarpMMA = 17;
 
 struct Layout {
-  static constexpr int QA = 0;
-  static constexpr int QB = QA + kBlockBytes;
-  static constexpr int K = QB + kBlockBytes;             // NS stages x 16 KB
+  static constexpr int Q = 0;                            // [2 bands][tile A, tile B] x 16 KB
+  static constexpr int K = Q + 4 * kBlockBytes;          // NS stages x 16 KB
   static constexpr int V = K + NS * kBlockBytes;         // NS stages x 16 KB
   static constexpr int BAR = V + NS * kBlockBytes;
-  static constexpr int kBars = 32;
+  static constexpr int kBars = 40;
   static constexpr int XCH = BAR + kBars * 8;            // float [2 parity][2 tile][2 half][128 rows]
   static constexpr int MISC = XCH + 2 * 2 * 2 * 128 * 4;
   static constexpr int TOTAL = MISC + 16;
@@ -385,14 +386,15 @@ struct Layout {
 
 namespace barriers {
 enum {
-  B_Q = 0,
-  B_KFULL = 1,                   // + stage (NS)
+  B_Q = 0,                       // + band parity: Q_A / Q_B of the band loaded
+  B_QFREE = B_Q + 2,             // + band parity: every S MMA of the band completed (its Q buffer is free)
+  B_KFULL = B_QFREE + 2,         // + stage (NS)
   B_VFULL = B_KFULL + NS,        // + stage
   B_KVEMPTY = B_VFULL + NS,      // + stage
   B_SFULL = B_KVEMPTY + NS,      // + slot: S of the slot's current job written
   B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
   B_PVDONE = B_TDONE + NSLOT,    // + slot: the PV that read the slot's P completed
-  B_ODONE = B_PVDONE + NSLOT,    // + 2 * tile + (j & 1): PV(tile, j) and every MMA before it completed
+  B_ODONE = B_PVDONE + NSLOT,    // + 2 * tile + (n & 1) for the tile's n-th PV: it and every MMA before it completed
   B_FINAL = B_ODONE + 4,
   B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
@@ -540,6 +542,63 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, ui
   tmem_st16(tP, pw);
 }
 
+// Band k of this CTA.  The grid is persistent (one CTA per SM) and takes the bands in rounds of gridDim.x:
+// round k covers the global band indices [k G, k G + G), in snake order (CTA c takes k G + c in even rounds,
+// k G + G - 1 - c in odd ones), which balances the band sizes across CTAs (the heaviest and lightest bands
+// of a (batch, head) alternate) while a round still covers whole runs of adjacent (batch, head) pairs, so
+// their K/V stay in L2.  Global band order: the bands of one (batch, head) back to back, heaviest first.
+struct BandInfo {
+  int b, h, q0;
+  Band bd;
+  int n_kv, n_jobs;
+};
+
+__device__ __forceinline__ bool band_info(int k, const Params& p, BandInfo& bi) {
+  const int n_bands = p.n_qt;
+  const int total = n_bands * p.B * p.H;
+  const int G = (int)gridDim.x;
+  const int lin = k * G + ((k & 1) ? (G - 1 - (int)blockIdx.x) : (int)blockIdx.x);
+  if (lin >= total) return false;
+  const int band = n_bands - 1 - lin % n_bands;
+  const int bh = lin / n_bands;
+  bi.b = bh / p.H;
+  bi.h = bh % p.H;
+  bi.q0 = band * 256;
+  bi.bd.nA = 2 * band + 1;                               // KV tiles 0..2*band (diagonal at 2*band)
+  bi.bd.nB = (bi.q0 + 128 < p.T) ? 2 * band + 2 : 0;     // KV tiles 0..2*band+1 (diagonal at 2*band+1)
+  bi.n_kv = bi.bd.nB ? bi.bd.nB : bi.bd.nA;
+  bi.n_jobs = bi.bd.jobs();
+  return true;
+}
+
+// Position in this CTA's job stream: job g of band k, with the counts of everything before that band.
+struct Cursor {
+  int k, g;
+  int jbase;      // jobs of earlier bands
+  int kvbase;     // K/V tiles of earlier bands
+  int pvbase[2];  // PVs of each tile in earlier bands
+  bool valid;
+  BandInfo bi;
+  __device__ __forceinline__ void init(const Params& p) {
+    k = 0;
+    g = 0;
+    jbase = 0;
+    kvbase = 0;
+    pvbase[0] = pvbase[1] = 0;
+    valid = band_info(0, p, bi);
+  }
+  __device__ __forceinline__ void next(const Params& p) {
+    if (++g < bi.n_jobs) return;
+    jbase += bi.n_jobs;
+    kvbase += bi.n_kv;
+    pvbase[0] += bi.bd.nA;
+    pvbase[1] += bi.bd.nB;
+    ++k;
+    g = 0;
+    valid = band_info(k, p, bi);
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -554,22 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // bands of one (batch, head) back to back, heaviest first (K/V reuse in L2)
-  const int n_bands = (p.T + 255) / 256;
-  const int lin = blockIdx.x;
-  const int band = n_bands - 1 - lin % n_bands;
-  const int bh = lin / n_bands;
-  const int b = bh / p.H;
-  const int h = bh % p.H;
-  const int q0 = band * 256;
-  Band bd;
-  bd.nA = 2 * band + 1;                          // KV tiles 0..2*band (diagonal at 2*band)
-  bd.nB = (q0 + 128 < p.T) ? 2 * band + 2 : 0;   // KV tiles 0..2*band+1 (diagonal at 2*band+1)
-  const int n_kv = bd.nB ? bd.nB : bd.nA;
-  const int n_jobs = bd.jobs();
-
   if (threadIdx.x == 0) {
-    mbar_init(bar(B_Q), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_Q + i), 1);
+      mbar_init(bar(B_QFREE + i), 1);
+    }
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar(B_KFULL + s), 1);
       mbar_init(bar(B_VFULL + s), 1);
@@ -597,32 +645,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpTMA) {
     // ------------------------------------------------------------ producer
+    // Q_A / Q_B of band k into Q buffer k & 1 (once the S MMAs of band k - 2 completed), then the band's K/V
+    // tiles into the ring, which runs on across bands.
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(bar(B_Q), (bd.nB ? 2 : 1) * 128 * D * 2);
-      tma_load_4d(sbase + L::QA, &tmQ, 0, q0, h, b, bar(B_Q));
-      if (bd.nB) tma_load_4d(sbase + L::QB, &tmQ, 0, q0 + 128, h, b, bar(B_Q));
+      int q_loads[2] = {0, 0};
       int last_use[NS];
       for (int s = 0; s < NS; ++s) last_use[s] = -1;
+      int kv = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % NS;
-        if (j >= NS) {
-          ok = mbar_wait(bar(B_KVEMPTY + s), ((j / NS) - 1) & 1, abort_flag, 21);
+      BandInfo bi;
+      for (int k = 0; ok && band_info(k, p, bi); ++k) {
+        const int qb = k & 1;
+        if (k >= 2) {
+          ok = mbar_wait(bar(B_QFREE + qb), ((k >> 1) - 1) & 1, abort_flag, 20);
           if (!ok) break;
         }
-        mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
-        tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, h, b, bar(B_KFULL + s));
-        mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
-        tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, h, b, bar(B_VFULL + s));
-        last_use[s] = j / NS;
+        const uint32_t qdst = sbase + L::Q + qb * 2 * kBlockBytes;
+        mbar_expect_tx(bar(B_Q + qb), (bi.bd.nB ? 2 : 1) * 128 * D * 2);
+        tma_load_4d(qdst, &tmQ, 0, bi.q0, bi.h, bi.b, bar(B_Q + qb));
+        if (bi.bd.nB) tma_load_4d(qdst + kBlockBytes, &tmQ, 0, bi.q0 + 128, bi.h, bi.b, bar(B_Q + qb));
+        ++q_loads[qb];
+        for (int j = 0; j < bi.n_kv; ++j, ++kv) {
+          const int s = kv % NS;
+          if (kv >= NS) {
+            ok = mbar_wait(bar(B_KVEMPTY + s), ((kv / NS) - 1) & 1, abort_flag, 21);
+            if (!ok) break;
+          }
+          mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
+          tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, bi.h, bi.b, bar(B_KFULL + s));
+          mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
+          tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, bi.h, bi.b, bar(B_VFULL + s));
+          last_use[s] = kv / NS;
+        }
       }
       if (!ok || *abort_flag) {
         // drain the copies still in flight before the CTA exits
         volatile int never = 0;
-        mbar_wait(bar(B_Q), 0, &never, 0);
+        for (int qb = 0; qb < 2; ++qb)
+          if (q_loads[qb] > 0) mbar_wait(bar(B_Q + qb), (q_loads[qb] - 1) & 1, &never, 0);
         for (int s = 0; s < NS; ++s) {
           if (last_use[s] >= 0) {
             mbar_wait(bar(B_KFULL + s), last_use[s] & 1, &never, 0);
@@ -633,43 +696,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMMA) {
     // ------------------------------------------------------------ MMA issuer
-    // S(0), S(1), S(2); then for each job g: PV(g) once its P is written, and S(g+3) into the same slot
-    // once that PV completed.  The whole warp runs the loop (operands stay warp-uniform); one elected lane
-    // issues each MMA and commit.
+    // One job stream over all of this CTA's bands: S of the first three jobs; then for each job G: PV(G) once
+    // its P is written, and S(G + 3) -- possibly of the next band -- into the same slot once that PV
+    // completed.  The whole warp runs the loop (operands stay warp-uniform); one elected lane issues each MMA
+    // and commit.
     constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
     constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
-    const uint64_t dqa = sw128_desc(sbase + L::QA, 16, 1024);
-    const uint64_t dqb = sw128_desc(sbase + L::QB, 16, 1024);
     const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
     const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
     auto wait_all = [&](int i, uint32_t parity, int site) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar(i), parity, abort_flag, site));
     };
-    auto issue_s = [&](int g) -> bool {
+    auto issue_s = [&](const Cursor& c) -> bool {
       int w, j;
-      bd.job(g, w, j);
-      const int s = j % NS;
-      if (!wait_all(B_KFULL + s, (j / NS) & 1, 23)) return false;
+      c.bi.bd.job(c.g, w, j);
+      if (c.g == 0 && !wait_all(B_Q + (c.k & 1), (c.k >> 1) & 1, 22)) return false;
+      const int kvg = c.kvbase + j;
+      const int s = kvg % NS;
+      if (!wait_all(B_KFULL + s, (kvg / NS) & 1, 23)) return false;
       tc_fence_after();
-      const uint64_t da = w ? dqb : dqa;
+      const uint64_t da = sw128_desc(sbase + L::Q + ((c.k & 1) * 2 + w) * kBlockBytes, 16, 1024);
       const uint64_t db = desc_add(dk0, s * kBlockBytes);
-      const uint32_t td = tmem + 128 * (g % NSLOT);
+      const int G = c.jbase + c.g;
+      const uint32_t td = tmem + 128 * (G % NSLOT);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
         umma_f16_ss_w(td, desc_add(da, kk * 32), desc_add(db, kk * 32), kIdescS, kk > 0 ? 1u : 0u);
-      umma_commit_w(bar(B_SFULL + g % NSLOT));
+      umma_commit_w(bar(B_SFULL + G % NSLOT));
+      if (c.g == c.bi.n_jobs - 1) umma_commit_w(bar(B_QFREE + (c.k & 1)));   // the band's last S
       return true;
     };
-    bool ok = wait_all(B_Q, 0, 22);
-    for (int g = 0; ok && g < NSLOT && g < n_jobs; ++g) ok = issue_s(g);
-    for (int g = 0; ok && g < n_jobs; ++g) {
+    Cursor cs, cp;
+    cs.init(p);
+    cp.init(p);
+    bool ok = true;
+    for (int i = 0; ok && i < NSLOT && cs.valid; ++i) {
+      ok = issue_s(cs);
+      cs.next(p);
+    }
+    while (ok && cp.valid) {
       int w, j;
-      bd.job(g, w, j);
-      const int slot = g % NSLOT;
-      const int s = j % NS;
-      ok = wait_all(B_TDONE + slot, (g / NSLOT) & 1, 24);
+      cp.bi.bd.job(cp.g, w, j);
+      const int G = cp.jbase + cp.g;
+      const int slot = G % NSLOT;
+      const int kvg = cp.kvbase + j;
+      const int s = kvg % NS;
+      ok = wait_all(B_TDONE + slot, (G / NSLOT) & 1, 24);
       if (!ok) break;
-      ok = wait_all(B_VFULL + s, (j / NS) & 1, 25);
+      ok = wait_all(B_VFULL + s, (kvg / NS) & 1, 25);
       if (!ok) break;
       tc_fence_after();
       const uint64_t db = desc_add(dv0, s * kBlockBytes);
@@ -678,14 +752,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk)   // keys 16kk.. : P columns p_col(8kk)..
         umma_f16_ts_w(td, ta + p_col(8 * kk), desc_add(db, kk * 16 * 128), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+      const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
       umma_commit_w(bar(B_PVDONE + slot));
-      umma_commit_w(bar(B_ODONE + 2 * w + (j & 1)));
-      if (bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
-      if (g + NSLOT < n_jobs) {
-        ok = wait_all(B_PVDONE + slot, (g / NSLOT) & 1, 26);
+      umma_commit_w(bar(B_ODONE + 2 * w + (pv & 1)));
+      if (cp.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
+      if (cs.valid) {
+        ok = wait_all(B_PVDONE + slot, (G / NSLOT) & 1, 26);
         if (!ok) break;
-        ok = issue_s(g + NSLOT);
+        ok = issue_s(cs);
+        cs.next(p);
       }
+      cp.next(p);
     }
     umma_commit_w(bar(B_FINAL));
     volatile int never = 0;
@@ -696,10 +773,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hf = (warp >> 2) & 1;            // score columns 64*hf .. 64*hf+63
     const int wq = warp & 3;                   // TMEM lane quarter
     const int row = wq * 32 + lane;
-    const int q_idx = q0 + 128 * w + row;
     const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
     const uint32_t tO = tmem + kColO + 64 * w + 32 * hf + t_lane;   // this half's 32 O columns
-    const int n_w = (w == 0) ? bd.nA : bd.nB;
     const float sl2 = p.scale_log2;
     float* xch = reinterpret_cast<float*>(smem + L::XCH);
     auto xslot = [&](int par, int half) -> float* { return xch + ((par * 2 + w) * 2 + half) * 128 + row; };
@@ -707,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t pair_phase = 0;
     // the two halves of these rows swap one value through shared memory (bounded mbarrier handshake); the
     // exchange slot alternates with the handshake count, so a value is never overwritten before it is read
-    auto swap = [&](float mine, int, bool& good) -> float {
+    auto swap = [&](float mine, bool& good) -> float {
       const int par = (int)(pair_phase & 1);
       *xslot(par, hf) = mine;
       mbar_arrive(pair);
@@ -715,109 +790,119 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++pair_phase;
       return *xslot(par, hf ^ 1);
     };
-    RowState st;
-    st.m = 0.f;
-    st.kr = 0.f;
-    st.l2 = f2_pack(0.f, 0.f);
-    bool ok = true;
+    // the n-th PV of this tile (over all bands) and every MMA before it completed
+    auto wait_pv = [&](int n, int site) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + 2 * w + (n & 1)), (n >> 1) & 1, abort_flag, site));
+    };
     const int pair_bar = 1 + 4 * w + wq;   // named barrier of the two warps that share these rows
-    for (int j = 0; j < n_w; ++j) {
-      // A failed (timed-out) wait poisons this warp: it skips the remaining work of the band but still takes
-      // every pair barrier below, so the other warp of the pair never waits on a barrier this one skips.
-      const int g = bd.job_of(w, j);
-      const int slot = g % NSLOT;
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (g / NSLOT) & 1, abort_flag, 28));
-      // O completion barriers alternate by tile parity, and each tile first waits for the PV two tiles
-      // back, so any later parity wait on them is never more than one phase behind
-      if (ok && j >= 2)
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + 2 * w + (j & 1)), ((j - 2) >> 1) & 1, abort_flag, 29));
-      const uint32_t tS = tmem + 128 * slot + t_lane;
-      const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
-      const int kbase = j * BN + 64 * hf;    // this half's first key
+    bool ok = true;
+    int jbase = 0, pvbase = 0;             // jobs of earlier bands, PVs of this tile in earlier bands
+    BandInfo bi;
+    for (int k = 0; band_info(k, p, bi); ++k) {
+      const Band bd = bi.bd;
+      const int q_idx = bi.q0 + 128 * w + row;
+      const int n_w = (w == 0) ? bd.nA : bd.nB;
+      RowState st;
+      st.m = 0.f;
       st.kr = 0.f;
-      if (ok) {
-        tc_fence_after();
-        const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
-        uint32_t r[32];
-        if (j == 0) {
-          // common reference max: the larger of the two halves' first-chunk maxima (key 0 is always visible)
-          tmem_ld32(tS + 64 * hf, r);
-          tmem_wait_ld32(r);
-          float mx = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (kbase + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
-          mx = fmaxf(mx, swap(mx, 1, ok));
-          st.m = mx * sl2;
-        }
+      st.l2 = f2_pack(0.f, 0.f);
+      for (int j = 0; j < n_w; ++j) {
+        // A failed (timed-out) wait poisons this warp: it skips the remaining work but still takes every pair
+        // barrier below, so the other warp of the pair never waits on a barrier this one skips.
+        const int G = jbase + bd.job_of(w, j);
+        const int slot = G % NSLOT;
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (G / NSLOT) & 1, abort_flag, 28));
+        // each tile first waits for its PV two jobs back, so a later parity wait on the alternating O
+        // barriers is never more than one phase behind
+        if (ok && j >= 2) ok = wait_pv(pvbase + j - 2, 29);
+        const uint32_t tS = tmem + 128 * slot + t_lane;
+        const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
+        const int kbase = j * BN + 64 * hf;    // this half's first key
+        st.kr = 0.f;
         if (ok) {
-#pragma unroll 1
-          for (int cc = 0; cc < 2; ++cc) {
-            tmem_ld32(tS + 64 * hf + 32 * cc, r);
+          tc_fence_after();
+          const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
+          uint32_t r[32];
+          if (j == 0) {
+            // common reference max: the larger of the two halves' first-chunk maxima (key 0 is always visible)
+            tmem_ld32(tS + 64 * hf, r);
             tmem_wait_ld32(r);
-            softmax_chunk(r, tP0 + 16 * cc, tP0, cc, kbase + 32 * cc, q_idx, sl2, diag, st);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (kbase + i <= q_idx) mx = fmaxf(mx, __uint_as_float(r[i]));
+            mx = fmaxf(mx, swap(mx, ok));
+            st.m = mx * sl2;
           }
-        }
-      }
-      // did either half of these rows raise m in this tile?  (a 64-thread barrier with an OR; the raises are
-      // exchanged through shared memory only when one did)
-      if (bar_red_or(pair_bar, 64, ok && st.kr > 0.0f) && ok) {
-        const float k_all = fmaxf(st.kr, swap(st.kr, 0, ok));
-        if (ok) {
-          tmem_wait_st();
-          const float fp = pow2_neg(k_all - st.kr);     // this half's P and l: from m + kr to m + k_all
-          scale_cols16<true>(tP0, fp);
-          scale_cols16<true>(tP0 + 16, fp);
-          float la, lb;
-          f2_unpack(st.l2, la, lb);
-          st.l2 = f2_pack(la * fp, lb * fp);
-          if (j > 0) {
-            // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
-            ok = __all_sync(0xffffffffu,
-                            mbar_wait(bar(B_ODONE + 2 * w + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, 32));
-            if (ok) {
-              tc_fence_after();
-              const float fo = pow2_neg(k_all);
-              scale_cols16<false>(tO, fo);
-              scale_cols16<false>(tO + 16, fo);
+          if (ok) {
+#pragma unroll 1
+            for (int cc = 0; cc < 2; ++cc) {
+              tmem_ld32(tS + 64 * hf + 32 * cc, r);
+              tmem_wait_ld32(r);
+              softmax_chunk(r, tP0 + 16 * cc, tP0, cc, kbase + 32 * cc, q_idx, sl2, diag, st);
             }
           }
-          st.m += k_all;
+        }
+        // did either half of these rows raise m in this tile?  (a 64-thread barrier with an OR; the raises
+        // are exchanged through shared memory only when one did)
+        if (bar_red_or(pair_bar, 64, ok && st.kr > 0.0f) && ok) {
+          const float k_all = fmaxf(st.kr, swap(st.kr, ok));
+          if (ok) {
+            tmem_wait_st();
+            const float fp = pow2_neg(k_all - st.kr);     // this half's P and l: from m + kr to m + k_all
+            scale_cols16<true>(tP0, fp);
+            scale_cols16<true>(tP0 + 16, fp);
+            float la, lb;
+            f2_unpack(st.l2, la, lb);
+            st.l2 = f2_pack(la * fp, lb * fp);
+            if (j > 0) {
+              // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
+              ok = wait_pv(pvbase + j - 1, 32);
+              if (ok) {
+                tc_fence_after();
+                const float fo = pow2_neg(k_all);
+                scale_cols16<false>(tO, fo);
+                scale_cols16<false>(tO + 16, fo);
+              }
+            }
+            st.m += k_all;
+          }
+        }
+        if (ok) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(B_TDONE + slot));
         }
       }
-      if (ok) {
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(B_TDONE + slot));
-      }
-    }
-    if (ok && n_w > 0) {
-      float la, lb;
-      f2_unpack(st.l2, la, lb);
-      const float l = la + lb;
-      const float l_all = l + swap(l, (n_w & 1), ok);
-      ok = ok && __all_sync(0xffffffffu,
-                            mbar_wait(bar(B_ODONE + 2 * w + ((n_w - 1) & 1)), ((n_w - 1) >> 1) & 1, abort_flag, 31));
-      if (ok) {
-        tc_fence_after();
-        const float inv_l = 1.0f / l_all;
-        uint32_t o[32];
-        tmem_ld32(tO, o);
-        tmem_wait_ld32(o);
-        if (q_idx < p.T) {
-          __nv_bfloat16* orow =
-              p.o + (int64_t)b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)h * p.os_h + 32 * hf;
+      if (ok && n_w > 0) {
+        float la, lb;
+        f2_unpack(st.l2, la, lb);
+        const float l = la + lb;
+        const float l_all = l + swap(l, ok);
+        ok = ok && wait_pv(pvbase + n_w - 1, 31);
+        if (ok) {
+          tc_fence_after();
+          const float inv_l = 1.0f / l_all;
+          uint32_t o[32];
+          tmem_ld32(tO, o);
+          tmem_wait_ld32(o);
+          if (q_idx < p.T) {
+            __nv_bfloat16* orow =
+                p.o + (int64_t)bi.b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)bi.h * p.os_h + 32 * hf;
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
-            v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
-            v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
-            v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + i) = v;
+            for (int i = 0; i < 32; i += 8) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+              v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+              v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+              v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + i) = v;
+            }
           }
         }
       }
+      jbase += bi.n_jobs;
+      pvbase += n_w;
     }
   }
 
@@ -886,8 +971,9 @@ static int launch_v2(const void* q, const void* k, const void* v, void* o, int B
   p.H = H;
   p.n_qt = (T + 255) / 256;
   p.scale_log2 = scale * 1.4426950408889634f;
-  const int64_t blocks = (int64_t)p.n_qt * B * H;
-  ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
+  const int64_t bands = (int64_t)p.n_qt * B * H;
+  ENGPT_REQUIRE(bands <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
+  const int64_t blocks = std::min<int64_t>(bands, num_sms());   // persistent: one CTA per SM
   auto kern = v2::attn_fwd2_kernel;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, v2::Layout::kDynSmem);
   if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "attention: smem attribute: %s", cudaGetErrorString(e));
