@@ -50,8 +50,11 @@ __device__ __forceinline__ RowScalars finish_row(const ResidualArgs& a, float rh
 template <int MAXCH, typename BT>
 __global__ void __launch_bounds__(256, (MAXCH <= 4 ? 3 : 1)) residual_vec_kernel(ResidualArgs a) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  if (row >= a.rows) return;
+  // rows from the last to the first: the GEMM that wrote the branch just before finished on its last rows,
+  // which are the ones still in L2
+  const int64_t rr = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (rr >= a.rows) return;
+  const int64_t row = a.rows - 1 - rr;
   const int nch = a.d >> 3;
   const float* yrow = a.y + row * a.d;
   const BT* brow = reinterpret_cast<const BT*>(a.branch) + row * a.d;
