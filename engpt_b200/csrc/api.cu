@@ -209,18 +209,29 @@ struct CastList {
   const float* src[kCastMax];
   __nv_bfloat16* dst[kCastMax];
   int64_t count[kCastMax];
+  int block0[kCastMax + 1];   // tensor i owns blocks [block0[i], block0[i + 1]) of the 1-D grid
+  int m;
 };
+
+constexpr int kCastVecPerThread = 4;   // 8-element vectors per thread and block-stride step
 
 // grid.y = tensor, grid.x strides over that tensor in 8-element chunks
 __global__ void __launch_bounds__(256) cast_many_kernel(const __grid_constant__ CastList L) {
-  const int t = blockIdx.y;
+  // this block's tensor: the last i with block0[i] <= blockIdx.x (blocks in proportion to the tensor sizes)
+  int lo = 0, hi = L.m - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (L.block0[mid] <= (int)blockIdx.x) lo = mid; else hi = mid - 1;
+  }
+  const int t = lo;
   const float* __restrict__ src = L.src[t];
   __nv_bfloat16* __restrict__ dst = L.dst[t];
   const int64_t n = L.count[t];
   const int64_t n8 = n / 8;
   const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int nb = L.block0[t + 1] - L.block0[t];
+  const int64_t stride = (int64_t)nb * blockDim.x;
+  const int64_t first = (int64_t)(blockIdx.x - L.block0[t]) * blockDim.x + threadIdx.x;
   if (vec) {
     for (int64_t e = first; e < n8; e += stride) {
       float4 a = *reinterpret_cast<const float4*>(src + e * 8);
@@ -491,7 +502,6 @@ int engpt_cast_f32_bf16_many(const void* const* src, void* const* dst, const int
   for (int base = 0; base < n; base += kCastMax) {
     const int m = (n - base) < kCastMax ? (n - base) : kCastMax;
     CastList L;
-    int64_t maxc = 0;
     for (int i = 0; i < m; ++i) {
       ENGPT_REQUIRE(counts[base + i] >= 0, ENGPT_ERR_SHAPE, "cast_many: count[%d] < 0", base + i);
       ENGPT_REQUIRE(counts[base + i] == 0 || (src[base + i] && dst[base + i]), ENGPT_ERR_ARG,
@@ -499,19 +509,26 @@ int engpt_cast_f32_bf16_many(const void* const* src, void* const* dst, const int
       L.src[i] = static_cast<const float*>(src[base + i]);
       L.dst[i] = static_cast<__nv_bfloat16*>(dst[base + i]);
       L.count[i] = counts[base + i];
-      if (L.count[i] > maxc) maxc = L.count[i];
     }
     for (int i = m; i < kCastMax; ++i) {
       L.src[i] = nullptr;
       L.dst[i] = nullptr;
       L.count[i] = 0;
     }
-    // enough blocks per tensor to fill the GPU with the whole batch in flight
-    int64_t per = (maxc / 8 + 255) / 256;
-    const int64_t cap = ((int64_t)num_sms() * 8 + m - 1) / m;
-    if (per > cap) per = cap;
-    if (per < 1) per = 1;
-    cast_many_kernel<<<dim3((unsigned)per, (unsigned)m), 256, 0, st>>>(L);
+    // blocks in proportion to each tensor's size (every tensor at least one), so the whole batch finishes
+    // together with the GPU full until the end
+    int64_t nblk = 0;
+    for (int i = 0; i < m; ++i) {
+      L.block0[i] = (int)nblk;
+      const int64_t vecs = (L.count[i] + 7) / 8;
+      int64_t b = (vecs + 256 * kCastVecPerThread - 1) / (256 * kCastVecPerThread);
+      if (b < 1) b = 1;
+      nblk += b;
+      ENGPT_REQUIRE(nblk <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "cast_many: too many blocks");
+    }
+    for (int i = m; i <= kCastMax; ++i) L.block0[i] = (int)nblk;
+    L.m = m;
+    cast_many_kernel<<<(unsigned)nblk, 256, 0, st>>>(L);
     int rc = check_launch("cast_f32_bf16_many");
     if (rc) return rc;
   }

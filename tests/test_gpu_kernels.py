@@ -277,6 +277,22 @@ def test_cast_f32_bf16_many_matches_torch(cuda):
         assert torch.equal(y, x.to(torch.bfloat16))
 
 
+def test_cast_f32_bf16_many_batches_and_sizes(cuda):
+    """More tensors than one launch takes (64), an empty one, and sizes from 1 element to 2M (blocks are handed
+    out in proportion to the sizes)."""
+    import ctypes
+    g = torch.Generator().manual_seed(5)
+    sizes = [0, 3, 2_000_001] + [(i * 7919) % 40000 + 1 for i in range(67)]
+    srcs = [torch.randn(n, generator=g).to(cuda) for n in sizes]
+    dsts = [torch.full(x.shape, 7.0, device=cuda, dtype=torch.bfloat16) for x in srcs]
+    n = len(srcs)
+    _lib.call("engpt_cast_f32_bf16_many", (ctypes.c_void_p * n)(*[x.data_ptr() for x in srcs]),
+              (ctypes.c_void_p * n)(*[x.data_ptr() for x in dsts]),
+              (ctypes.c_int64 * n)(*[x.numel() for x in srcs]), n, _lib.stream_handle(cuda))
+    for x, y in zip(srcs, dsts):
+        assert torch.equal(y, x.to(torch.bfloat16))
+
+
 @pytest.mark.parametrize("V", [1001, 50257])
 def test_cross_entropy_vs_oracle(cuda, V):
     from engpt_b200 import EfficientNGPT
