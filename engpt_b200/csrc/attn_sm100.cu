@@ -365,7 +365,7 @@ namespace v2 {
 
 constexpr int D = 64;
 constexpr int BN = 128;              // keys per KV tile
-constexpr int NS = 3;                // K/V pipeline stages
+constexpr int NS = 4;                // K/V pipeline stages
 constexpr int NSLOT = 3;             // TMEM score slots
 constexpr int kSoftmaxWarps = 16;
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;   // warps 0-15 softmax, 16 TMA, 17 MMA
