@@ -388,9 +388,8 @@ namespace barriers {
 enum {
   B_Q = 0,                       // + band parity: Q_A / Q_B of the band loaded
   B_QFREE = B_Q + 2,             // + band parity: every S MMA of the band completed (its Q buffer is free)
-  B_KFULL = B_QFREE + 2,         // + stage (NS)
-  B_VFULL = B_KFULL + NS,        // + stage
-  B_KVEMPTY = B_VFULL + NS,      // + stage
+  B_KVFULL = B_QFREE + 2,        // + stage (NS): the stage's K and V tiles loaded
+  B_KVEMPTY = B_KVFULL + NS,     // + stage
   B_SFULL = B_KVEMPTY + NS,      // + slot: S of the slot's current job written
   B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
   B_PVDONE = B_TDONE + NSLOT,    // + slot: the PV that read the slot's P completed
@@ -619,8 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_QFREE + i), 1);
     }
     for (int s = 0; s < NS; ++s) {
-      mbar_init(bar(B_KFULL + s), 1);
-      mbar_init(bar(B_VFULL + s), 1);
+      mbar_init(bar(B_KVFULL + s), 1);
       mbar_init(bar(B_KVEMPTY + s), 1);
     }
     for (int s = 0; s < NSLOT; ++s) {
@@ -674,10 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = mbar_wait(bar(B_KVEMPTY + s), ((kv / NS) - 1) & 1, abort_flag, 21);
             if (!ok) break;
           }
-          mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
-          tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, bi.h, bi.b, bar(B_KFULL + s));
-          mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
-          tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, bi.h, bi.b, bar(B_VFULL + s));
+          mbar_expect_tx(bar(B_KVFULL + s), 2 * BN * D * 2);
+          tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, bi.h, bi.b, bar(B_KVFULL + s));
+          tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, bi.h, bi.b, bar(B_KVFULL + s));
           last_use[s] = kv / NS;
         }
       }
@@ -687,10 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int qb = 0; qb < 2; ++qb)
           if (q_loads[qb] > 0) mbar_wait(bar(B_Q + qb), (q_loads[qb] - 1) & 1, &never, 0);
         for (int s = 0; s < NS; ++s) {
-          if (last_use[s] >= 0) {
-            mbar_wait(bar(B_KFULL + s), last_use[s] & 1, &never, 0);
-            mbar_wait(bar(B_VFULL + s), last_use[s] & 1, &never, 0);
-          }
+          if (last_use[s] >= 0) mbar_wait(bar(B_KVFULL + s), last_use[s] & 1, &never, 0);
         }
       }
     }
@@ -699,7 +693,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // One job stream over all of this CTA's bands: S of the first three jobs; then for each job G: PV(G) once
     // its P is written, and S(G + 3) -- possibly of the next band -- into the same slot once that PV
     // completed.  The whole warp runs the loop (operands stay warp-uniform); one elected lane issues each MMA
-    // and commit.
+    // and commit.  This warp is the kernel's critical path, so it waits only where it must: a stage's K and V
+    // complete one barrier, waited once by the first S that reads the stage.
     constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
     constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
     const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
@@ -707,13 +702,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_all = [&](int i, uint32_t parity, int site) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar(i), parity, abort_flag, site));
     };
+    int kv_waited = -1;   // K/V tiles up to this one are known loaded (the jobs' tiles never go back)
     auto issue_s = [&](const Cursor& c) -> bool {
       int w, j;
       c.bi.bd.job(c.g, w, j);
       if (c.g == 0 && !wait_all(B_Q + (c.k & 1), (c.k >> 1) & 1, 22)) return false;
       const int kvg = c.kvbase + j;
       const int s = kvg % NS;
-      if (!wait_all(B_KFULL + s, (kvg / NS) & 1, 23)) return false;
+      if (kvg > kv_waited) {
+        if (!wait_all(B_KVFULL + s, (kvg / NS) & 1, 23)) return false;
+        kv_waited = kvg;
+      }
       tc_fence_after();
       const uint64_t da = sw128_desc(sbase + L::Q + ((c.k & 1) * 2 + w) * kBlockBytes, 16, 1024);
       const uint64_t db = desc_add(dk0, s * kBlockBytes);
@@ -739,11 +738,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       cp.bi.bd.job(cp.g, w, j);
       const int G = cp.jbase + cp.g;
       const int slot = G % NSLOT;
-      const int kvg = cp.kvbase + j;
-      const int s = kvg % NS;
+      const int s = (cp.kvbase + j) % NS;   // loaded: this job's S (issued before, by this warp) waited for it
       ok = wait_all(B_TDONE + slot, (G / NSLOT) & 1, 24);
-      if (!ok) break;
-      ok = wait_all(B_VFULL + s, (kvg / NS) & 1, 25);
       if (!ok) break;
       tc_fence_after();
       const uint64_t db = desc_add(dv0, s * kBlockBytes);
