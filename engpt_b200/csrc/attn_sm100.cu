@@ -392,8 +392,7 @@ enum {
   B_KVEMPTY = B_KVFULL + NS,     // + stage
   B_SFULL = B_KVEMPTY + NS,      // + slot: S of the slot's current job written
   B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
-  B_PVDONE = B_TDONE + NSLOT,    // + slot: the PV that read the slot's P completed
-  B_ODONE = B_PVDONE + NSLOT,    // + 2 * tile + (n & 1) for the tile's n-th PV: it and every MMA before it completed
+  B_ODONE = B_TDONE + NSLOT,     // + 2 * tile + (n & 1) for the tile's n-th PV: it and every MMA before it completed
   B_FINAL = B_ODONE + 4,
   B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
@@ -624,7 +623,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(bar(B_SFULL + s), 1);
       mbar_init(bar(B_TDONE + s), 256);
-      mbar_init(bar(B_PVDONE + s), 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(bar(B_ODONE + i), 1);
     mbar_init(bar(B_FINAL), 1);
@@ -749,11 +747,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = 0; kk < BN / 16; ++kk)   // keys 16kk.. : P columns p_col(8kk)..
         umma_f16_ts_w(td, ta + p_col(8 * kk), desc_add(db, kk * 16 * 128), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
       const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
-      umma_commit_w(bar(B_PVDONE + slot));
       umma_commit_w(bar(B_ODONE + 2 * w + (pv & 1)));
       if (cp.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
       if (cs.valid) {
-        ok = wait_all(B_PVDONE + slot, (G / NSLOT) & 1, 26);
+        // this PV (the last reader of the slot's P) completed: S(G + 3) may overwrite the slot.  The tile's
+        // next PV on this barrier is issued by this warp only later, so the parity wait is unambiguous.
+        ok = wait_all(B_ODONE + 2 * w + (pv & 1), (pv >> 1) & 1, 26);
         if (!ok) break;
         ok = issue_s(cs);
         cs.next(p);
