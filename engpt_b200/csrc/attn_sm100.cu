@@ -807,9 +807,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int G = jbase + bd.job_of(w, j);
         const int slot = G % NSLOT;
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (G / NSLOT) & 1, abort_flag, 28));
-        // each tile first waits for its PV two jobs back, so a later parity wait on the alternating O
-        // barriers is never more than one phase behind
-        if (ok && j >= 2) ok = wait_pv(pvbase + j - 2, 29);
         const uint32_t tS = tmem + 128 * slot + t_lane;
         const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
         const int kbase = j * BN + 64 * hf;    // this half's first key
@@ -851,8 +848,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             f2_unpack(st.l2, la, lb);
             st.l2 = f2_pack(la * fp, lb * fp);
             if (j > 0) {
-              // O (every earlier PV of this tile, relative to m) scales by 2^-k_all
-              ok = wait_pv(pvbase + j - 1, 32);
+              // O (every earlier PV of this tile, relative to m) scales by 2^-k_all.  The O barriers alternate
+              // by PV parity: the PV two back completing first (it and all MMAs before it) keeps the parity wait
+              // on PV j - 1 from seeing an older phase.
+              if (j >= 2) ok = wait_pv(pvbase + j - 2, 29);
+              ok = ok && wait_pv(pvbase + j - 1, 32);
               if (ok) {
                 tc_fence_after();
                 const float fo = pow2_neg(k_all);
@@ -874,6 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         f2_unpack(st.l2, la, lb);
         const float l = la + lb;
         const float l_all = l + swap(l, ok);
+        if (n_w >= 2) ok = ok && wait_pv(pvbase + n_w - 2, 30);   // as above: the PV two back first
         ok = ok && wait_pv(pvbase + n_w - 1, 31);
         if (ok) {
           tc_fence_after();
