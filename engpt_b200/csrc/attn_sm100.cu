@@ -540,6 +540,50 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, ui
   tmem_st16(tP, pw);
 }
 
+// The 8 MMAs of one PV (keys 16kk.., kk = 0..7: P columns p_col(8kk) = 0, 8, 16, 24, 64, 72, 80, 88 of the
+// slot, V rows 16kk.. at 2048-byte steps of the descriptor) and the 4 of one S (K16 steps: 32 bytes into the
+// 128-byte swizzled rows of Q and K), each group issued under one warp election.
+__device__ __forceinline__ void umma_pv8_w(uint32_t td, uint32_t ta, uint64_t db, uint32_t idesc, uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred e, p, t;\n\t.reg .b64 d;\n\t.reg .b32 a;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 t, %4, %4;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.s64 d, %2, 128;\n\tadd.u32 a, %1, 8;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 256;\n\tadd.u32 a, %1, 16;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 384;\n\tadd.u32 a, %1, 24;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 512;\n\tadd.u32 a, %1, 64;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 640;\n\tadd.u32 a, %1, 72;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 768;\n\tadd.u32 a, %1, 80;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
+      "add.s64 d, %2, 896;\n\tadd.u32 a, %1, 88;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t}" ::"r"(td),
+      "r"(ta), "l"(db), "r"(idesc), "r"(acc0)
+      : "memory");
+}
+__device__ __forceinline__ void umma_s4_w(uint32_t td, uint64_t da, uint64_t db, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, f, t;\n\t.reg .b64 x, y;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 f, %3, %3;\n\t"
+      "setp.eq.b32 t, %3, %3;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
+      "add.s64 x, %1, 2;\n\tadd.s64 y, %2, 2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t"
+      "add.s64 x, %1, 4;\n\tadd.s64 y, %2, 4;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t"
+      "add.s64 x, %1, 6;\n\tadd.s64 y, %2, 6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t}" ::"r"(td),
+      "l"(da), "l"(db), "r"(idesc)
+      : "memory");
+}
+
 // Band k of this CTA.  The grid is persistent (one CTA per SM) and takes the bands in rounds of gridDim.x:
 // round k covers the global band indices [k G, k G + G), in snake order (CTA c takes k G + c in even rounds,
 // k G + G - 1 - c in odd ones), which balances the band sizes across CTAs (the heaviest and lightest bands
@@ -716,9 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t db = desc_add(dk0, s * kBlockBytes);
       const int G = c.jbase + c.g;
       const uint32_t td = tmem + 128 * (G % NSLOT);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        umma_f16_ss_w(td, desc_add(da, kk * 32), desc_add(db, kk * 32), kIdescS, kk > 0 ? 1u : 0u);
+      umma_s4_w(td, da, db, kIdescS);
       umma_commit_w(bar(B_SFULL + G % NSLOT));
       if (c.g == c.bi.n_jobs - 1) umma_commit_w(bar(B_QFREE + (c.k & 1)));   // the band's last S
       return true;
@@ -743,9 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t db = desc_add(dv0, s * kBlockBytes);
       const uint32_t ta = tmem + 128 * slot;
       const uint32_t td = tmem + kColO + 64 * w;
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk)   // keys 16kk.. : P columns p_col(8kk)..
-        umma_f16_ts_w(td, ta + p_col(8 * kk), desc_add(db, kk * 16 * 128), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+      umma_pv8_w(td, ta, db, kIdescPV, j > 0 ? 1u : 0u);
       const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
       umma_commit_w(bar(B_ODONE + 2 * w + (pv & 1)));
       if (cp.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
