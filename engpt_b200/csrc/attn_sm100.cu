@@ -343,10 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // 128-column score slots that the jobs rotate through (job g uses slot g % 3)
 // and the two O accumulators (64 columns each).  The softmax turns a slot's
 // fp32 scores S into bf16 P in place and the PV MMA reads P from TMEM, so the
-// softmax never touches shared memory.  With three slots the MMA warp computes
-// the next S of a tile while that tile's softmax is still exponentiating the
-// current one; a slot is refilled only after the PV that read its P completed
-// (waited on its own mbarrier: tcgen05 orders MMAs only within one accumulator).
+// softmax never touches shared memory.  With three slots the next S of a tile
+// is computed while that tile's softmax is still exponentiating the current
+// one; a slot is refilled only after the PV that read its P completed (PFREE:
+// tcgen05 orders MMAs only within one accumulator).  S and PV MMAs come from
+// two single-thread issuers (warps 17 and 18, on different SM sub-partitions),
+// so a PV is issued as soon as its P is written, never behind an S issue or
+// the wait for a slot; K and V have separate barriers, released by the last S
+// and the last PV that read them.
 //
 // Softmax: 16 warps, 4 per SM sub-partition.  A tile's 128 rows are shared by
 // 8 warps: warp (tile, half, quarter) owns TMEM lanes 32*quarter.. and the
@@ -368,16 +372,17 @@ constexpr int BN = 128;              // keys per KV tile
 constexpr int NS = 4;                // K/V pipeline stages
 constexpr int NSLOT = 3;             // TMEM score slots
 constexpr int kSoftmaxWarps = 16;
-constexpr int kThreads = (kSoftmaxWarps + 2) * 32;   // warps 0-15 softmax, 16 TMA, 17 MMA
+constexpr int kThreads = (kSoftmaxWarps + 3) * 32;   // warps 0-15 softmax, 16 TMA, 17 S MMAs, 18 PV MMAs
 constexpr int kWarpTMA = 16;
-constexpr int kWarpMMA = 17;
+constexpr int kWarpS = 17;
+constexpr int kWarpPV = 18;
 
 struct Layout {
   static constexpr int Q = 0;                            // [2 bands][tile A, tile B] x 16 KB
   static constexpr int K = Q + 4 * kBlockBytes;          // NS stages x 16 KB
   static constexpr int V = K + NS * kBlockBytes;         // NS stages x 16 KB
   static constexpr int BAR = V + NS * kBlockBytes;
-  static constexpr int kBars = 40;
+  static constexpr int kBars = 48;
   static constexpr int XCH = BAR + kBars * 8;            // float [2 parity][2 tile][2 half][128 rows]
   static constexpr int MISC = XCH + 2 * 2 * 2 * 128 * 4;
   static constexpr int TOTAL = MISC + 16;
@@ -388,12 +393,15 @@ namespace barriers {
 enum {
   B_Q = 0,                       // + band parity: Q_A / Q_B of the band loaded
   B_QFREE = B_Q + 2,             // + band parity: every S MMA of the band completed (its Q buffer is free)
-  B_KVFULL = B_QFREE + 2,        // + stage (NS): the stage's K and V tiles loaded
-  B_KVEMPTY = B_KVFULL + NS,     // + stage
-  B_SFULL = B_KVEMPTY + NS,      // + slot: S of the slot's current job written
+  B_KFULL = B_QFREE + 2,         // + stage (NS): the stage's K tile loaded
+  B_VFULL = B_KFULL + NS,        // + stage: the stage's V tile loaded
+  B_KEMPTY = B_VFULL + NS,       // + stage: the last S that reads the stage's K tile completed
+  B_VEMPTY = B_KEMPTY + NS,      // + stage: the last PV that reads the stage's V tile completed
+  B_SFULL = B_VEMPTY + NS,       // + slot: S of the slot's current job written
   B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
-  B_ODONE = B_TDONE + NSLOT,     // + 2 * tile + (n & 1) for the tile's n-th PV: it and every MMA before it completed
-  B_FINAL = B_ODONE + 4,
+  B_PFREE = B_TDONE + NSLOT,     // + slot: the PV of the slot's current job (and every PV before it) completed
+  B_ODONE = B_PFREE + NSLOT,     // + 2 * tile + (n & 1) for the tile's n-th PV: it and every PV before it completed
+  B_FINAL = B_ODONE + 4,         // every MMA of both issuers completed (2 arrivals)
   B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
 }  // namespace barriers
@@ -540,50 +548,6 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, ui
   tmem_st16(tP, pw);
 }
 
-// The 8 MMAs of one PV (keys 16kk.., kk = 0..7: P columns p_col(8kk) = 0, 8, 16, 24, 64, 72, 80, 88 of the
-// slot, V rows 16kk.. at 2048-byte steps of the descriptor) and the 4 of one S (K16 steps: 32 bytes into the
-// 128-byte swizzled rows of Q and K), each group issued under one warp election.
-__device__ __forceinline__ void umma_pv8_w(uint32_t td, uint32_t ta, uint64_t db, uint32_t idesc, uint32_t acc0) {
-  asm volatile(
-      "{\n\t.reg .pred e, p, t;\n\t.reg .b64 d;\n\t.reg .b32 a;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "setp.eq.b32 t, %4, %4;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
-      "add.s64 d, %2, 128;\n\tadd.u32 a, %1, 8;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 256;\n\tadd.u32 a, %1, 16;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 384;\n\tadd.u32 a, %1, 24;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 512;\n\tadd.u32 a, %1, 64;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 640;\n\tadd.u32 a, %1, 72;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 768;\n\tadd.u32 a, %1, 80;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t"
-      "add.s64 d, %2, 896;\n\tadd.u32 a, %1, 88;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], d, %3, t;\n\t}" ::"r"(td),
-      "r"(ta), "l"(db), "r"(idesc), "r"(acc0)
-      : "memory");
-}
-__device__ __forceinline__ void umma_s4_w(uint32_t td, uint64_t da, uint64_t db, uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .pred e, f, t;\n\t.reg .b64 x, y;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 f, %3, %3;\n\t"
-      "setp.eq.b32 t, %3, %3;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
-      "add.s64 x, %1, 2;\n\tadd.s64 y, %2, 2;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t"
-      "add.s64 x, %1, 4;\n\tadd.s64 y, %2, 4;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t"
-      "add.s64 x, %1, 6;\n\tadd.s64 y, %2, 6;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], x, y, %3, t;\n\t}" ::"r"(td),
-      "l"(da), "l"(db), "r"(idesc)
-      : "memory");
-}
-
 // Band k of this CTA.  The grid is persistent (one CTA per SM) and takes the bands in rounds of gridDim.x:
 // round k covers the global band indices [k G, k G + G), in snake order (CTA c takes k G + c in even rounds,
 // k G + G - 1 - c in odd ones), which balances the band sizes across CTAs (the heaviest and lightest bands
@@ -661,20 +625,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_QFREE + i), 1);
     }
     for (int s = 0; s < NS; ++s) {
-      mbar_init(bar(B_KVFULL + s), 1);
-      mbar_init(bar(B_KVEMPTY + s), 1);
+      mbar_init(bar(B_KFULL + s), 1);
+      mbar_init(bar(B_VFULL + s), 1);
+      mbar_init(bar(B_KEMPTY + s), 1);
+      mbar_init(bar(B_VEMPTY + s), 1);
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(bar(B_SFULL + s), 1);
       mbar_init(bar(B_TDONE + s), 256);
+      mbar_init(bar(B_PFREE + s), 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(bar(B_ODONE + i), 1);
-    mbar_init(bar(B_FINAL), 1);
+    mbar_init(bar(B_FINAL), 2);
     for (int i = 0; i < 8; ++i) mbar_init(bar(B_PAIR + i), 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kWarpMMA) {
+  if (warp == kWarpS) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
     tc_fence_before();
@@ -711,12 +678,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < bi.n_kv; ++j, ++kv) {
           const int s = kv % NS;
           if (kv >= NS) {
-            ok = mbar_wait(bar(B_KVEMPTY + s), ((kv / NS) - 1) & 1, abort_flag, 21);
+            ok = mbar_wait(bar(B_KEMPTY + s), ((kv / NS) - 1) & 1, abort_flag, 21) &&
+                 mbar_wait(bar(B_VEMPTY + s), ((kv / NS) - 1) & 1, abort_flag, 25);
             if (!ok) break;
           }
-          mbar_expect_tx(bar(B_KVFULL + s), 2 * BN * D * 2);
-          tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, bi.h, bi.b, bar(B_KVFULL + s));
-          tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, bi.h, bi.b, bar(B_KVFULL + s));
+          mbar_expect_tx(bar(B_KFULL + s), BN * D * 2);
+          tma_load_4d(sbase + L::K + s * kBlockBytes, &tmK, 0, j * BN, bi.h, bi.b, bar(B_KFULL + s));
+          mbar_expect_tx(bar(B_VFULL + s), BN * D * 2);
+          tma_load_4d(sbase + L::V + s * kBlockBytes, &tmV, 0, j * BN, bi.h, bi.b, bar(B_VFULL + s));
           last_use[s] = kv / NS;
         }
       }
@@ -726,82 +695,94 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int qb = 0; qb < 2; ++qb)
           if (q_loads[qb] > 0) mbar_wait(bar(B_Q + qb), (q_loads[qb] - 1) & 1, &never, 0);
         for (int s = 0; s < NS; ++s) {
-          if (last_use[s] >= 0) mbar_wait(bar(B_KVFULL + s), last_use[s] & 1, &never, 0);
+          if (last_use[s] >= 0) {
+            mbar_wait(bar(B_KFULL + s), last_use[s] & 1, &never, 0);
+            mbar_wait(bar(B_VFULL + s), last_use[s] & 1, &never, 0);
+          }
         }
       }
     }
-  } else if (warp == kWarpMMA) {
-    // ------------------------------------------------------------ MMA issuer
-    // One job stream over all of this CTA's bands: S of the first three jobs; then for each job G: PV(G) once
-    // its P is written, and S(G + 3) -- possibly of the next band -- into the same slot once that PV
-    // completed.  The whole warp runs the loop (operands stay warp-uniform); one elected lane issues each MMA
-    // and commit.  This warp is the kernel's critical path, so it waits only where it must: a stage's K and V
-    // complete one barrier, waited once by the first S that reads the stage.
-    constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
-    constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
-    const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
-    const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
-    auto wait_all = [&](int i, uint32_t parity, int site) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar(i), parity, abort_flag, site));
-    };
-    int kv_waited = -1;   // K/V tiles up to this one are known loaded (the jobs' tiles never go back)
-    auto issue_s = [&](const Cursor& c) -> bool {
-      int w, j;
-      c.bi.bd.job(c.g, w, j);
-      if (c.g == 0 && !wait_all(B_Q + (c.k & 1), (c.k >> 1) & 1, 22)) return false;
-      const int kvg = c.kvbase + j;
-      const int s = kvg % NS;
-      if (kvg > kv_waited) {
-        if (!wait_all(B_KVFULL + s, (kvg / NS) & 1, 23)) return false;
-        kv_waited = kvg;
-      }
-      tc_fence_after();
-      const uint64_t da = sw128_desc(sbase + L::Q + ((c.k & 1) * 2 + w) * kBlockBytes, 16, 1024);
-      const uint64_t db = desc_add(dk0, s * kBlockBytes);
-      const int G = c.jbase + c.g;
-      const uint32_t td = tmem + 128 * (G % NSLOT);
-      umma_s4_w(td, da, db, kIdescS);
-      umma_commit_w(bar(B_SFULL + G % NSLOT));
-      if (c.g == c.bi.n_jobs - 1) umma_commit_w(bar(B_QFREE + (c.k & 1)));   // the band's last S
-      return true;
-    };
-    Cursor cs, cp;
-    cs.init(p);
-    cp.init(p);
-    bool ok = true;
-    for (int i = 0; ok && i < NSLOT && cs.valid; ++i) {
-      ok = issue_s(cs);
-      cs.next(p);
-    }
-    while (ok && cp.valid) {
-      int w, j;
-      cp.bi.bd.job(cp.g, w, j);
-      const int G = cp.jbase + cp.g;
-      const int slot = G % NSLOT;
-      const int s = (cp.kvbase + j) % NS;   // loaded: this job's S (issued before, by this warp) waited for it
-      ok = wait_all(B_TDONE + slot, (G / NSLOT) & 1, 24);
-      if (!ok) break;
-      tc_fence_after();
-      const uint64_t db = desc_add(dv0, s * kBlockBytes);
-      const uint32_t ta = tmem + 128 * slot;
-      const uint32_t td = tmem + kColO + 64 * w;
-      umma_pv8_w(td, ta, db, kIdescPV, j > 0 ? 1u : 0u);
-      const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
-      umma_commit_w(bar(B_ODONE + 2 * w + (pv & 1)));
-      if (cp.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_KVEMPTY + s));   // last job that reads K_j / V_j
-      if (cs.valid) {
-        // this PV (the last reader of the slot's P) completed: S(G + 3) may overwrite the slot.  The tile's
-        // next PV on this barrier is issued by this warp only later, so the parity wait is unambiguous.
-        ok = wait_all(B_ODONE + 2 * w + (pv & 1), (pv >> 1) & 1, 26);
-        if (!ok) break;
-        ok = issue_s(cs);
+  } else if (warp == kWarpS) {
+    // ------------------------------------------------------------ S issuer
+    // One thread walks the job stream over all of this CTA's bands and issues S(G) = Q K_j^T into slot G % 3
+    // once the PV that read P(G - 3) from that slot completed.  The S and PV issuers are separate threads, so neither's
+    // waits and issue latency delay the other; tcgen05 MMAs of different threads are unordered, which is
+    // fine: S and PV share no accumulator, and every hand-off between them goes through the softmax.
+    if (lane == 0) {
+      constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
+      const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
+      int k_waited = -1;   // K tiles up to this one are known loaded (the jobs' tiles never go back)
+      Cursor cs;
+      cs.init(p);
+      while (cs.valid) {
+        int w, j;
+        cs.bi.bd.job(cs.g, w, j);
+        const int G = cs.jbase + cs.g;
+        const int slot = G % NSLOT;
+        // PV(G - 3) completed; the slot's next PFREE phase needs PV(G), which needs S(G), issued below
+        if (G >= NSLOT && !mbar_wait(bar(B_PFREE + slot), ((G / NSLOT) - 1) & 1, abort_flag, 26)) break;
+        if (cs.g == 0 && !mbar_wait(bar(B_Q + (cs.k & 1)), (cs.k >> 1) & 1, abort_flag, 22)) break;
+        const int kvg = cs.kvbase + j;
+        const int s = kvg % NS;
+        if (kvg > k_waited) {
+          if (!mbar_wait(bar(B_KFULL + s), (kvg / NS) & 1, abort_flag, 23)) break;
+          k_waited = kvg;
+        }
+        tc_fence_after();
+        const uint64_t da = sw128_desc(sbase + L::Q + ((cs.k & 1) * 2 + w) * kBlockBytes, 16, 1024);
+        const uint64_t db = desc_add(dk0, s * kBlockBytes);
+        const uint32_t td = tmem + 128 * slot;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) umma_f16_ss(td, da + 2 * kk, db + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
+        umma_commit(bar(B_SFULL + slot));
+        if (cs.bi.bd.nB == 0 || w == 1) umma_commit(bar(B_KEMPTY + s));          // last S that reads K_j
+        if (cs.g == cs.bi.n_jobs - 1) umma_commit(bar(B_QFREE + (cs.k & 1)));   // the band's last S
         cs.next(p);
       }
-      cp.next(p);
+      umma_commit(bar(B_FINAL));
+      volatile int never = 0;
+      mbar_wait(bar(B_FINAL), 0, &never, 27);
     }
-    umma_commit_w(bar(B_FINAL));
-    volatile int never = 0;
-    mbar_wait(bar(B_FINAL), 0, &never, 27);
+    __syncwarp();
+  } else if (warp == kWarpPV) {
+    // ------------------------------------------------------------ PV issuer
+    // One thread issues O_tile += P(G) V_j for each job G once the softmax wrote P(G).
+    if (lane == 0) {
+      constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
+      const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
+      int v_waited = -1;
+      Cursor cp;
+      cp.init(p);
+      while (cp.valid) {
+        int w, j;
+        cp.bi.bd.job(cp.g, w, j);
+        const int G = cp.jbase + cp.g;
+        const int slot = G % NSLOT;
+        const int kvg = cp.kvbase + j;
+        const int s = kvg % NS;
+        if (kvg > v_waited) {
+          if (!mbar_wait(bar(B_VFULL + s), (kvg / NS) & 1, abort_flag, 35)) break;
+          v_waited = kvg;
+        }
+        // P(G) written; the slot's next TDONE phase needs S(G + 3), which waits for this PV
+        if (!mbar_wait(bar(B_TDONE + slot), (G / NSLOT) & 1, abort_flag, 24)) break;
+        tc_fence_after();
+        const uint64_t db = desc_add(dv0, s * kBlockBytes);
+        const uint32_t ta = tmem + 128 * slot;
+        const uint32_t td = tmem + kColO + 64 * w;
+        // keys 16kk..16kk+15: P columns p_col(8kk) of the slot, V rows 16kk.. (2048 bytes apart)
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ts(td, ta + p_col(8 * kk), db + 128 * kk, kIdescPV, (kk > 0 || j > 0) ? 1u : 0u);
+        const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
+        umma_commit(bar(B_ODONE + 2 * w + (pv & 1)));
+        umma_commit(bar(B_PFREE + slot));
+        if (cp.bi.bd.nB == 0 || w == 1) umma_commit(bar(B_VEMPTY + s));          // last PV that reads V_j
+        cp.next(p);
+      }
+      umma_commit(bar(B_FINAL));
+    }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
     const int w = warp >> 3;                   // 0: tile A, 1: tile B
@@ -944,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMMA) {
+  if (warp == kWarpS) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
