@@ -363,7 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // handshake), the half that raised less rescales its P, and O is rescaled
 // (each half its 32 columns) after the previous PV completed.  Every stored
 // value stays <= 2^8 and the final O / l is exact.  Fully masked chunks of a
-// diagonal tile are written as zeros without exponentiating.
+// diagonal tile are written as zeros without exponentiating.  A band's O / l
+// is stored after the first job of the tile's next band (its P written), so
+// the wait for the band's last PV overlaps that job; the PV that starts the
+// next band's O waits for the load of the old one (OREAD).
 // ============================================================================
 namespace v2 {
 
@@ -384,7 +387,8 @@ struct Layout {
   static constexpr int BAR = V + NS * kBlockBytes;
   static constexpr int kBars = 48;
   static constexpr int XCH = BAR + kBars * 8;            // float [2 parity][2 tile][2 half][128 rows]
-  static constexpr int MISC = XCH + 2 * 2 * 2 * 128 * 4;
+  static constexpr int LSUM = XCH + 2 * 2 * 2 * 128 * 4; // float [2 tile][2 half][128 rows]: a band's row sum l
+  static constexpr int MISC = LSUM + 2 * 2 * 128 * 4;
   static constexpr int TOTAL = MISC + 16;
   static constexpr int kDynSmem = TOTAL + 1024;
 };
@@ -402,7 +406,8 @@ enum {
   B_PFREE = B_TDONE + NSLOT,     // + slot: the PV of the slot's current job (and every PV before it) completed
   B_ODONE = B_PFREE + NSLOT,     // + 2 * tile + (n & 1) for the tile's n-th PV: it and every PV before it completed
   B_FINAL = B_ODONE + 4,         // every MMA of both issuers completed (2 arrivals)
-  B_PAIR = B_FINAL + 1           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
+  B_OREAD = B_FINAL + 1,         // + tile: the softmax loaded the tile's O of its previous band (256 arrivals)
+  B_PAIR = B_OREAD + 2           // + 4 * tile + quarter: the two halves of those rows (64 arrivals)
 };
 }  // namespace barriers
 using namespace barriers;
@@ -637,6 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 4; ++i) mbar_init(bar(B_ODONE + i), 1);
     mbar_init(bar(B_FINAL), 2);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(B_OREAD + i), 256);
     for (int i = 0; i < 8; ++i) mbar_init(bar(B_PAIR + i), 64);
     *abort_flag = 0;
     fence_mbar_init();
@@ -751,6 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
       const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
       int v_waited = -1;
+      int bands_w[2] = {0, 0};   // bands of each tile with jobs so far
       Cursor cp;
       cp.init(p);
       while (cp.valid) {
@@ -766,6 +773,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // P(G) written; the slot's next TDONE phase needs S(G + 3), which waits for this PV
         if (!mbar_wait(bar(B_TDONE + slot), (G / NSLOT) & 1, abort_flag, 24)) break;
+        if (j == 0) {
+          // this PV starts the tile's O afresh: the softmax loaded O of the tile's previous band.  The next
+          // OREAD phase of the tile needs this band's PVs, so the parity wait is unambiguous.
+          if (bands_w[w] > 0 && !mbar_wait(bar(B_OREAD + w), (bands_w[w] - 1) & 1, abort_flag, 36)) break;
+          ++bands_w[w];
+        }
         tc_fence_after();
         const uint64_t db = desc_add(dv0, s * kBlockBytes);
         const uint32_t ta = tmem + 128 * slot;
@@ -813,6 +826,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pair_bar = 1 + 4 * w + wq;   // named barrier of the two warps that share these rows
     bool ok = true;
     int jbase = 0, pvbase = 0;             // jobs of earlier bands, PVs of this tile in earlier bands
+    float* lsum = reinterpret_cast<float*>(smem + L::LSUM) + (w * 2 + hf) * 128 + row;   // this thread's l
+    int pend_k = -1, pend_n = 0;           // band whose O is still to be stored, and its PV count
+    // O / l of band pk of this tile, whose last PV is this tile's PV pvbase - 1 (no later PV of the tile is
+    // issued before OREAD): wait for that PV, load O, release the accumulator and store the rows.  It runs
+    // after the first job of the next band (or after the last band), so that job's S, exponentials and P
+    // overlap the wait for the band's last PV.
+    auto store_band = [&](int pk, int n_pk) {
+      BandInfo eb;
+      band_info(pk, p, eb);
+      const int qe = eb.q0 + 128 * w + row;
+      if (n_pk >= 2) ok = ok && wait_pv(pvbase - 2, 30);   // as below: the PV two back first
+      ok = ok && wait_pv(pvbase - 1, 31);
+      if (ok) {
+        tc_fence_after();
+        uint32_t o[32];
+        tmem_ld32(tO, o);
+        tmem_wait_ld32(o);
+        tc_fence_before();
+        mbar_arrive(bar(B_OREAD + w));
+        const float inv_l = 1.0f / *lsum;
+        if (qe < p.T) {
+          __nv_bfloat16* orow =
+              p.o + (int64_t)eb.b * p.os_b + (int64_t)qe * p.os_t + (int64_t)eb.h * p.os_h + 32 * hf;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + i) = v;
+          }
+        }
+      }
+    };
     BandInfo bi;
     for (int k = 0; band_info(k, p, bi); ++k) {
       const Band bd = bi.bd;
@@ -889,38 +937,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(bar(B_TDONE + slot));
         }
+        if (j == 0 && pend_k >= 0) {   // the previous band's O, now that this band's first P is written
+          store_band(pend_k, pend_n);
+          pend_k = -1;
+        }
       }
       if (ok && n_w > 0) {
         float la, lb;
         f2_unpack(st.l2, la, lb);
         const float l = la + lb;
-        const float l_all = l + swap(l, ok);
-        if (n_w >= 2) ok = ok && wait_pv(pvbase + n_w - 2, 30);   // as above: the PV two back first
-        ok = ok && wait_pv(pvbase + n_w - 1, 31);
-        if (ok) {
-          tc_fence_after();
-          const float inv_l = 1.0f / l_all;
-          uint32_t o[32];
-          tmem_ld32(tO, o);
-          tmem_wait_ld32(o);
-          if (q_idx < p.T) {
-            __nv_bfloat16* orow =
-                p.o + (int64_t)bi.b * p.os_b + (int64_t)q_idx * p.os_t + (int64_t)bi.h * p.os_h + 32 * hf;
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[i + 0]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
-              v.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
-              v.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
-              v.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + i) = v;
-            }
-          }
-        }
+        *lsum = l + swap(l, ok);
+        pend_k = k;
+        pend_n = n_w;
       }
       jbase += bi.n_jobs;
       pvbase += n_w;
     }
+    if (pend_k >= 0) store_band(pend_k, pend_n);
   }
 
   tc_fence_before();
