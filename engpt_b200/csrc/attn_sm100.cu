@@ -401,8 +401,11 @@ enum {
   B_VFULL = B_KFULL + NS,        // + stage: the stage's V tile loaded
   B_KEMPTY = B_VFULL + NS,       // + stage: the last S that reads the stage's K tile completed
   B_VEMPTY = B_KEMPTY + NS,      // + stage: the last PV that reads the stage's V tile completed
-  B_SFULL = B_VEMPTY + NS,       // + slot: S of the slot's current job written
-  B_TDONE = B_SFULL + NSLOT,     // + slot: P of the slot's current job written (256 arrivals)
+  // + NSLOT * tile + slot: S of the tile's latest job in the slot written.  Each tile counts its own phases: a
+  // tile with no rows in a band skips that band's jobs, and on a barrier shared by both tiles its next wait
+  // could find the slot two phases behind and pass on the parity of an old phase.
+  B_SFULL = B_VEMPTY + NS,
+  B_TDONE = B_SFULL + 2 * NSLOT, // + slot: P of the slot's current job written (256 arrivals)
   B_PFREE = B_TDONE + NSLOT,     // + slot: the PV of the slot's current job (and every PV before it) completed
   B_ODONE = B_PFREE + NSLOT,     // + 2 * tile + (n & 1) for the tile's n-th PV: it and every PV before it completed
   B_FINAL = B_ODONE + 4,         // every MMA of both issuers completed (2 arrivals)
@@ -637,6 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(bar(B_SFULL + s), 1);
+      mbar_init(bar(B_SFULL + NSLOT + s), 1);
       mbar_init(bar(B_TDONE + s), 256);
       mbar_init(bar(B_PFREE + s), 1);
     }
@@ -740,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t td = tmem + 128 * slot;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) umma_f16_ss(td, da + 2 * kk, db + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
-        umma_commit(bar(B_SFULL + slot));
+        umma_commit(bar(B_SFULL + NSLOT * w + slot));
         if (cs.bi.bd.nB == 0 || w == 1) umma_commit(bar(B_KEMPTY + s));          // last S that reads K_j
         if (cs.g == cs.bi.n_jobs - 1) umma_commit(bar(B_QFREE + (cs.k & 1)));   // the band's last S
         cs.next(p);
@@ -828,6 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int jbase = 0, pvbase = 0;             // jobs of earlier bands, PVs of this tile in earlier bands
     float* lsum = reinterpret_cast<float*>(smem + L::LSUM) + (w * 2 + hf) * 128 + row;   // this thread's l
     int pend_k = -1, pend_n = 0;           // band whose O is still to be stored, and its PV count
+    uint32_t sphase = 0;                   // bit s: parity of this tile's next phase of SFULL slot s
     // O / l of band pk of this tile, whose last PV is this tile's PV pvbase - 1 (no later PV of the tile is
     // issued before OREAD): wait for that PV, load O, release the accumulator and store the rows.  It runs
     // after the first job of the next band (or after the last band), so that job's S, exponentials and P
@@ -875,7 +880,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // barrier below, so the other warp of the pair never waits on a barrier this one skips.
         const int G = jbase + bd.job_of(w, j);
         const int slot = G % NSLOT;
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + slot), (G / NSLOT) & 1, abort_flag, 28));
+        // this tile's previous job in the slot was waited for here, and its next one needs PV of this job (the
+        // slot's reuse waits for the PV three jobs back, and PVs are issued in job order): the wait is unambiguous
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + NSLOT * w + slot), (sphase >> slot) & 1u, abort_flag, 28));
+        sphase ^= 1u << slot;
         const uint32_t tS = tmem + 128 * slot + t_lane;
         const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
         const int kbase = j * BN + 64 * hf;    // this half's first key

@@ -180,6 +180,29 @@ def test_attention_tcgen05_bf16_vs_oracle(cuda, D, T):
     assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
 
 
+@pytest.mark.parametrize("B,T,H", [(8, 1152, 16), (2, 2048, 16)])
+def test_attention_tcgen05_many_bands_per_cta(cuda, B, T, H):
+    """More 256-query bands than SMs, so every CTA of the persistent head_dim-64 kernel walks several bands:
+    the Q double buffer, the job / K-V / PV counters that run across bands, the band store deferred past the
+    next band's first job, and (T = 1152) last bands whose second 128-row tile is empty.  Reference: torch's
+    fp32 causal SDPA on the same bf16-rounded inputs; bound as in the oracle test above."""
+    D = 64
+    q, k, v = _attn_inputs(B, T, H, D, seed=B * T + H)
+    qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
+    o = K.causal_sdpa(qb, kb, vb, scale=math.sqrt(D), dropout_p=0.0, impl="tcgen05")
+
+    def sdpa(x, y, z):
+        return torch.nn.functional.scaled_dot_product_attention(
+            x.transpose(1, 2), y.transpose(1, 2), z.transpose(1, 2), is_causal=True, scale=math.sqrt(D)
+        ).transpose(1, 2)
+
+    ref = sdpa(qb.float(), kb.float(), vb.float())
+    err = (o.float() - ref).abs().max().item()
+    err_torch = (sdpa(qb, kb, vb).float() - ref).abs().max().item()
+    assert err < 1.5e-2, (err, err_torch)
+    assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_attention_tcgen05_head_major_strides_and_unnormalised_inputs(cuda, D):
     # general (not unit-norm) q/k exercise the reference-max raising path; head-major strides exercise TMA maps
