@@ -2,7 +2,10 @@
 
 Usage (needs the Pi-Willie/enGPT sources, not needed at test time)::
 
-    PYTHONPATH=/root/reference python tests/golden/make_golden.py
+    PYTHONPATH=<enGPT checkout> python tests/golden/make_golden.py [name ...]
+
+With names (ops, small, attn, cfg1, cfg4, cfg3, cfg5) only those fixtures are
+written; with none, all of them.
 
 The reference is run on the CPU (fp64 for the op-level and small-model
 vectors, fp32 for the BASELINE-sized configs) with the seeds listed below.
@@ -122,7 +125,13 @@ def model_small(EfficientNGPT, ModelConfig):
 
 
 def model_config(EfficientNGPT, ModelConfig, name, *, V, L, H, d, T, B, state_layers, row_stride):
-    """A BASELINE-sized config in fp32: weights from torch.manual_seed(0) (CPU), ids from Generator(0)."""
+    """A BASELINE-sized config in fp32: weights from torch.manual_seed(0) (CPU), ids from Generator(0).
+
+    Stored: the loss, every token's log-sum-exp and target logit, weight
+    fingerprints, and for the listed layers the represented state Y/rho of
+    sequence 0 at every row_stride-th token plus rho of every token of
+    sequence 0.  The first 64 vocabulary logits of sequence 0 are stored for
+    T <= 256 only (they are 32 KB per 128 tokens)."""
     cfg = ModelConfig(vocab_size=V, block_size=T, n_layer=L, n_head=H, n_embd=d, mlp_ratio=4.0, dropout=0.0)
     torch.manual_seed(0)
     model = EfficientNGPT(cfg)
@@ -137,8 +146,10 @@ def model_config(EfficientNGPT, ModelConfig, name, *, V, L, H, d, T, B, state_la
     out = {"idx": idx.numpy().astype(np.int32), "targets": targets.numpy().astype(np.int32),
            "loss": np.float64(loss.item()), "w_names": names, "w_fp": fp,
            "lse": torch.logsumexp(logits.double(), dim=-1).numpy().astype(np.float32),
-           "logits_b0_v64": logits[0, :, :64].numpy(), "state_rows": rows,
+           "state_rows": rows,
            "state_layers": np.array(state_layers, dtype=np.int32)}
+    if T <= 256:
+        out["logits_b0_v64"] = logits[0, :, :64].numpy()
     # logits at the target positions for every token (what the loss reads).
     out["logits_at_target"] = logits.gather(-1, targets.unsqueeze(-1))[..., 0].numpy()
     for i in state_layers:
@@ -174,13 +185,23 @@ def isolated_attention(K):
 def main():
     EfficientNGPT, ModelConfig, K = _ref()
     torch.set_num_threads(os.cpu_count() or 1)
-    ops_vectors(K)
-    model_small(EfficientNGPT, ModelConfig)
-    isolated_attention(K)
-    model_config(EfficientNGPT, ModelConfig, "cfg1", V=50257, L=4, H=4, d=256, T=256, B=16,
-                 state_layers=[0, 1, 2, 3], row_stride=16)
-    model_config(EfficientNGPT, ModelConfig, "cfg4_deep", V=50257, L=128, H=4, d=256, T=256, B=16,
-                 state_layers=list(range(0, 128, 8)) + [127], row_stride=32)
+    jobs = {
+        "ops": lambda: ops_vectors(K),
+        "small": lambda: model_small(EfficientNGPT, ModelConfig),
+        "attn": lambda: isolated_attention(K),
+        "cfg1": lambda: model_config(EfficientNGPT, ModelConfig, "cfg1", V=50257, L=4, H=4, d=256, T=256, B=16,
+                                     state_layers=[0, 1, 2, 3], row_stride=16),
+        "cfg4": lambda: model_config(EfficientNGPT, ModelConfig, "cfg4_deep", V=50257, L=128, H=4, d=256, T=256,
+                                     B=16, state_layers=list(range(0, 128, 8)) + [127], row_stride=32),
+        # the benchmarked forward (L=16, d=1024, H=16, T=2048), two of its sequences
+        "cfg3": lambda: model_config(EfficientNGPT, ModelConfig, "cfg3_d1024", V=50257, L=16, H=16, d=1024, T=2048,
+                                     B=2, state_layers=[0, 3, 7, 11, 15], row_stride=128),
+        # the long-context prefill forward (L=24, d=2048, head_dim 128, T=8192), one sequence
+        "cfg5": lambda: model_config(EfficientNGPT, ModelConfig, "cfg5_d2048", V=50257, L=24, H=16, d=2048, T=8192,
+                                     B=1, state_layers=[0, 5, 11, 17, 23], row_stride=1024),
+    }
+    for name in (sys.argv[1:] or list(jobs)):
+        jobs[name]()
 
 
 if __name__ == "__main__":

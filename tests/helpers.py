@@ -10,6 +10,9 @@ CFG1 = dict(vocab_size=50257, block_size=256, n_layer=4, n_head=4, n_embd=256, m
 CFG1_BT = (16, 256)
 CFG4 = dict(vocab_size=50257, block_size=256, n_layer=128, n_head=4, n_embd=256, mlp_ratio=4.0, dropout=0.0)
 CFG4_BT = (16, 256)
+# the benchmarked forward and the long-context prefill forward
+CFG3 = dict(vocab_size=50257, block_size=2048, n_layer=16, n_head=16, n_embd=1024, mlp_ratio=4.0, dropout=0.0)
+CFG5 = dict(vocab_size=50257, block_size=8192, n_layer=24, n_head=16, n_embd=2048, mlp_ratio=4.0, dropout=0.0)
 SMALL = dict(vocab_size=32, block_size=12, n_layer=2, n_head=2, n_embd=32, mlp_ratio=2.0, dropout=0.0,
              alpha_init=0.1)
 

@@ -11,7 +11,7 @@ import torch
 
 from engpt_b200 import EfficientNGPT, ModelConfig, _lib
 from oracle import ngpt_oracle as O
-from tests.helpers import CFG1, CFG4, SMALL, row_rel_err, seeded_model, state_numpy
+from tests.helpers import CFG1, CFG3, CFG4, CFG5, SMALL, row_rel_err, seeded_model, state_numpy
 
 pytestmark = pytest.mark.gpu
 
@@ -107,6 +107,41 @@ def test_cfg4_deep_stack_fp32(golden, cuda):
     g, _, logits, loss, states = _cfg_run(golden, cuda, "cfg4_deep.npz", CFG4, bf16=False)
     _check_states(g, states, 1e-4)
     assert abs(loss.item() - float(g["loss"])) < 1e-4
+
+
+def _check_cfg_loss_lse(g, logits, loss, loss_tol, lse_tol):
+    assert abs(loss.item() - float(g["loss"])) < loss_tol, (loss.item(), float(g["loss"]))
+    lse = torch.logsumexp(logits.float(), dim=-1).double().cpu().numpy()
+    assert np.abs(lse - g["lse"]).max() < lse_tol
+
+
+def test_cfg3_benchmarked_forward_bf16_matches_reference(golden, cuda):
+    """The benchmarked forward (L=16, d=1024, H=16, T=2048; default engine: fused QKV GEMM, persistent tcgen05
+    attention, fused up/gate + SwiGLU, fused head + cross-entropy) on two of its sequences against the reference's
+    fp32 forward: Y/rho of 16 rows of sequence 0 at layers 0/3/7/11/15 within 2e-2, the loss within 1e-3."""
+    g, model, logits, loss, states = _cfg_run(golden, cuda, "cfg3_d1024.npz", CFG3, bf16=True)
+    worst = _check_states(g, states, BF16_TOL)
+    _check_cfg_loss_lse(g, logits, loss, LOSS_TOL, 0.1)
+    for i in g["state_layers"]:
+        np.testing.assert_allclose(states[i][1][0].cpu().numpy(), g[f"rho{i}"], rtol=2e-2)
+    print("cfg3 bf16 worst row-relative Y/rho error", worst, "loss", loss.item(), float(g["loss"]))
+
+
+def test_cfg3_benchmarked_forward_fp32_matches_reference(golden, cuda):
+    """The same configuration in fp32 (CUDA-core attention, fp32 GEMMs): Y/rho within 1e-5."""
+    g, model, logits, loss, states = _cfg_run(golden, cuda, "cfg3_d1024.npz", CFG3, bf16=False)
+    worst = _check_states(g, states, FP32_TOL)
+    _check_cfg_loss_lse(g, logits, loss, 1e-4, 2e-4)
+    print("cfg3 fp32 worst row-relative Y/rho error", worst)
+
+
+def test_cfg5_long_context_bf16_matches_reference(golden, cuda):
+    """Long-context prefill (L=24, d=2048, H=16, head_dim 128, T=8192), one sequence, bf16 engine against the
+    reference's fp32 forward: Y/rho of 8 rows at layers 0/5/11/17/23 within 2e-2, the loss within 1e-3."""
+    g, model, logits, loss, states = _cfg_run(golden, cuda, "cfg5_d2048.npz", CFG5, bf16=True)
+    worst = _check_states(g, states, BF16_TOL)
+    _check_cfg_loss_lse(g, logits, loss, LOSS_TOL, 0.1)
+    print("cfg5 bf16 worst row-relative Y/rho error", worst, "loss", loss.item(), float(g["loss"]))
 
 
 def test_forward_carried_general_rho_vs_oracle(cuda):

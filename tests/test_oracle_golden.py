@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from oracle import ngpt_oracle as O
-from tests.helpers import CFG1, CFG4, SMALL, fingerprint, row_rel_err, seeded_model, state_numpy
+from tests.helpers import CFG1, CFG3, CFG4, SMALL, fingerprint, row_rel_err, seeded_model, state_numpy
 
 
 def test_rotary_tables_match_reference(golden):
@@ -102,7 +102,7 @@ def test_small_model_init_matches_reference(golden):
         np.testing.assert_array_equal(v.numpy(), ref[k])
 
 
-@pytest.mark.parametrize("name,cfg", [("cfg1.npz", CFG1), ("cfg4_deep.npz", CFG4)])
+@pytest.mark.parametrize("name,cfg", [("cfg1.npz", CFG1), ("cfg4_deep.npz", CFG4), ("cfg3_d1024.npz", CFG3)])
 def test_seeded_init_fingerprint_matches_reference(golden, name, cfg):
     g = golden(name)
     model = seeded_model(cfg, seed=0)
