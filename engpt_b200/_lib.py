@@ -38,8 +38,10 @@ SIGNATURES = {
     "engpt_abi_version": (_i, []),
     "engpt_device_status": (_i, []),
     "engpt_clear_device_status": (_i, []),
+    "engpt_selftest_wait_timeout": (_i, [_i64, _p, _p]),
     "engpt_qkv_postprocess": (_i, [_p, _i, _p, _p, _p, _i, _p, _f, _f, _i, _i, _i, _i, _p, _p, _p, _i, _p]),
     "engpt_causal_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _i, _p]),
+    "engpt_ngpt_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _p, _f, _p]),
     "engpt_carried_residual_gauge": (_i, [_p, _p, _p, _i, _p, _f, _i, _f, _f, _f, _i64, _i, _p, _p, _p, _i, _p]),
     "engpt_rotary_tables": (_i, [_i, _i, _f, _p, _p, _p]),
     "engpt_embed_carried": (_i, [_p, _p, _i64, _i, _i64, _p, _p, _p, _p]),
@@ -100,6 +102,23 @@ def device_status() -> int:
 
 def clear_device_status() -> None:
     call("engpt_clear_device_status")
+
+
+def raise_on_device_status(clear: bool = True) -> None:
+    """Raise ``EngptError`` if a kernel recorded a failure (synchronises the device).
+
+    The word holds the first failure since it was last cleared: an
+    out-of-range token id or target (argument error) or a device wait that
+    ran out (timeout), with the site that recorded it.  With ``clear`` the
+    word is reset before raising, so the next check reports new failures only.
+    """
+    v = device_status()
+    if v == 0:
+        return
+    if clear:
+        clear_device_status()
+    code, site = v & 0xFF, v >> 8
+    raise EngptError("device status", code, f"recorded by a kernel at site {site} (word {v:#x})")
 
 
 def stream_handle(device: Optional[torch.device] = None) -> int:

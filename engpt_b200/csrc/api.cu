@@ -6,7 +6,6 @@
 
 #include <string.h>
 
-#include <mutex>
 
 namespace engpt {
 
@@ -563,27 +562,17 @@ int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, int64_t voc
 // library's device memory (one copy per device that loads the library).
 static __device__ __align__(256) float g_ce_noalloc_rows[ENGPT_CE_NOALLOC_MAX_ROWS];
 
-// Device address of g_ce_noalloc_rows per device.  In host code the array's
-// name is only a host-side stand-in, never a device address, so the address is
-// looked up once per device with that device current.
-static float* g_ce_noalloc_addr[64] = {nullptr};
-static std::mutex g_ce_noalloc_mu;
-
+// Device address of g_ce_noalloc_rows on the current device.  In host code the
+// array's name is only a host-side stand-in, never a device address, so the
+// address is looked up with the device current.  It is looked up on every
+// call (a cheap runtime query once the module is loaded) rather than cached,
+// so it stays valid across a cudaDeviceReset that rebuilds the context.
 static int ce_noalloc_scratch(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "cross_entropy_noalloc: cudaGetDevice: %s",
-                                         cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return set_error(ENGPT_ERR_UNSUPPORTED, "cross_entropy_noalloc: device %d", dev);
-  std::lock_guard<std::mutex> lock(g_ce_noalloc_mu);
-  if (g_ce_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_ce_noalloc_rows);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(ENGPT_ERR_LAUNCH, "cross_entropy_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_ce_noalloc_addr[dev] = static_cast<float*>(p);
-  }
-  *out = g_ce_noalloc_addr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_ce_noalloc_rows);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(ENGPT_ERR_LAUNCH, "cross_entropy_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  *out = static_cast<float*>(p);
   return ENGPT_OK;
 }
 

@@ -71,9 +71,14 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with `parity` to complete.  Gives up when the
-// shared abort word is set by another role, or after kWaitLimitNs, in which
-// case it records ENGPT_ERR_TIMEOUT(site) and raises the abort word.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+// CTA's shared abort word is set by another role of the same CTA, or after
+// limit_ns, in which case it records ENGPT_ERR_TIMEOUT(site) in the device
+// status word and raises the abort word.  The device status word itself is
+// not consulted: it may hold a failure of an earlier launch (or an argument
+// error such as an out-of-range target), and every wait of these kernels is
+// fed by the same CTA, so another CTA's failure cannot leave it waiting.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site,
+                                                uint64_t limit_ns) {
 #pragma unroll 1
   for (int i = 0; i < 4; ++i)
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
@@ -81,14 +86,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
-    // another role of this CTA gave up, or another CTA recorded a failure: leave quickly
-    if (*abort_flag || *reinterpret_cast<volatile int*>(&g_device_status)) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (*abort_flag) return false;   // another role of this CTA gave up: leave quickly
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_device_error(ENGPT_ERR_TIMEOUT, site);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+  return mbar_wait_limit(bar, parity, abort_flag, site, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------ clusters
@@ -147,7 +155,9 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait_cluster(bar, parity, 100000u)) return true;
-    if (*abort_flag || *reinterpret_cast<volatile int*>(&g_device_status)) return false;
+    // a peer CTA of this cluster that gave up sends no more messages: this wait then runs out on its own
+    // limit (the status word is not consulted, as in mbar_wait_limit)
+    if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       record_device_error(ENGPT_ERR_TIMEOUT, site);
       *abort_flag = 1;
@@ -387,6 +397,18 @@ __device__ __forceinline__ void tmem_wait_ld16(uint32_t* r) {
 // for, so the compiler cannot schedule their first use above the wait.
 __device__ __forceinline__ void tmem_wait_ld32(uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+// No instruction: ties 32 registers written by an earlier tcgen05.ld to this point of the (volatile) asm order,
+// so that, placed after a tcgen05.wait::ld, no use of them is scheduled above the wait.
+__device__ __forceinline__ void reg_fence32(uint32_t* r) {
+  asm volatile(""
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                  "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
                  "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),

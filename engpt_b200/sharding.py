@@ -112,6 +112,9 @@ def forward_sharded(forward: Callable[[Tensor, Optional[Tensor]], Tuple[Tensor, 
     """
     rank, world = _world(group)
     B = idx.shape[0]
+    if gather_logits and B < world:
+        # every rank sees the same global batch, so every rank raises here, before any collective
+        raise ValueError(f"gather_logits needs at least one row per rank (batch {B} < world size {world})")
     my_idx = shard_rows(idx, rank, world)
     my_tgt = shard_rows(targets, rank, world) if targets is not None else None
     if my_idx.shape[0] > 0:
@@ -123,6 +126,4 @@ def forward_sharded(forward: Callable[[Tensor, Optional[Tensor]], Tuple[Tensor, 
         out_loss = combine_loss(loss, valid_targets(my_tgt), device=idx.device, group=group)
     if not gather_logits:
         return logits, out_loss
-    if logits is None:
-        raise ValueError("gather_logits needs at least one row per rank (batch >= world size)")
     return gather_rows(logits, B, group=group), out_loss

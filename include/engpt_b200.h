@@ -76,12 +76,26 @@ ENGPT_API int engpt_abi_version(void);
 
 /*
  * Device-side error word of the current device: 0 when no kernel has
- * recorded a failure; otherwise the code of the first bounded wait that ran
- * out (ENGPT_ERR_TIMEOUT) with the site in the upper bits.  Synchronises the
- * device.  engpt_clear_device_status() resets it.
+ * recorded a failure; otherwise the first failure recorded, its engpt_status
+ * code in bits 0-7 and its site in the upper bits: ENGPT_ERR_TIMEOUT for a
+ * bounded wait that ran out, ENGPT_ERR_ARG for an out-of-range token id or
+ * target.  Synchronises the device.  engpt_clear_device_status() resets it.
+ * A set word does not change what later launches compute.
  */
 ENGPT_API int engpt_device_status(void);
 ENGPT_API int engpt_clear_device_status(void);
+
+/*
+ * Failure-path self-test (no counterpart in the reference, which has no
+ * device-side waits): one CTA whose first wait, on an mbarrier nothing
+ * arrives on, runs out after limit_ns (0 < limit_ns <= 1 s) and records
+ * ENGPT_ERR_TIMEOUT with site 99 in the device status word; a second role
+ * of the same CTA waiting on another such barrier leaves through the CTA's
+ * abort word.  flags_out (2 device ints) receives 1 for each wait that
+ * reported failure.  The kernel returns normally and the context stays
+ * usable; the caller clears the status word afterwards.
+ */
+ENGPT_API int engpt_selftest_wait_timeout(int64_t limit_ns, int* flags_out, void* stream);
 
 /*
  * qkv_postprocess_from_carried -- engpt/kernels.py:139-179.
@@ -111,6 +125,26 @@ ENGPT_API int engpt_qkv_postprocess(const void* qkv, int dtype, const float* rho
 ENGPT_API int engpt_causal_attention(const void* q, const void* k, const void* v, void* o,
                            int dtype, int B, int T, int H, int Dh, float scale,
                            const int64_t* strides, int impl, void* stream);
+
+/*
+ * causal_sdpa as the nGPT block calls it -- engpt/models.py:143-151 (q, k from
+ * qkv_postprocess_from_carried, engpt/kernels.py:139-179, then causal_sdpa
+ * engpt/kernels.py:417-431 with scale sqrt(Dh), engpt/kernels.py:434-435).
+ *
+ * Same arguments as engpt_causal_attention plus the effective score scales:
+ * q and k of head h must be unit vectors (per head) multiplied elementwise
+ * by qk_scale[h, :] * qk_mult (qk_scale [H, Dh] fp32 on the device), which is
+ * what the QKV post-process produces.  Then every score satisfies
+ * |q.k| <= max_i (qk_scale[h, i] qk_mult)^2, and the head_dim-64 bf16 kernel
+ * exponentiates against that fixed per-head bound instead of a running row
+ * maximum (no rescaling of P, l or O).  The bound is read on the device (no
+ * host synchronisation).  A head whose bound exceeds 48 in log2 units
+ * (scale * log2(e) * max s^2) runs the running-max softmax, as do other head
+ * dims and fp32 (the engpt_causal_attention kernels).
+ */
+ENGPT_API int engpt_ngpt_attention(const void* q, const void* k, const void* v, void* o, int dtype, int B, int T,
+                                   int H, int Dh, float scale, const int64_t* strides, const float* qk_scale,
+                                   float qk_mult, void* stream);
 
 /*
  * carried_residual_gauge -- engpt/kernels.py:277-324 (with the unfused pair
@@ -255,8 +289,9 @@ ENGPT_API int engpt_cross_entropy(const void* logits, int dtype, int64_t rows, i
  * library's device memory; every GPU that loads the library holds it until the
  * process exits.  More rows than that are rejected with ENGPT_ERR_SHAPE.
  *
- * The first call on each device looks up the array's device address (with
- * that device current); make that first call before any stream capture.
+ * Every call looks up the array's device address on the current device (the
+ * first call on a device may load the library's device code there); make
+ * that first call before any stream capture.
  * All calls share the one array and it keeps the last call's contents; each
  * call writes every entry it reads, so nothing needs clearing.  Calls that
  * overlap on the GPU (other streams, other threads) race on the array.

@@ -65,11 +65,18 @@ def _worker(rank, world, port, weights, idx, targets, out_dir):
     try:
         fwd = _oracle_forward(weights, O.OracleConfig(**SMALL))
         logits, loss = sharding.forward_sharded(fwd, torch.from_numpy(idx), torch.from_numpy(targets))
+        # batch 1 < world 2 with a logits gather: every rank raises before any collective (no rank is left
+        # waiting in the all-gather), and the group stays usable for the call after it
+        try:
+            sharding.forward_sharded(fwd, torch.from_numpy(idx[:1]), torch.from_numpy(targets[:1]))
+            raised = False
+        except ValueError:
+            raised = True
         # an empty shard on the last rank: loss only, no gather
         _, loss1 = sharding.forward_sharded(fwd, torch.from_numpy(idx[:1]), torch.from_numpy(targets[:1]),
                                             gather_logits=False)
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=logits.numpy(), loss=loss.item(),
-                 loss1=loss1.item())
+                 loss1=loss1.item(), raised=raised)
     finally:
         dist.destroy_process_group()
 
@@ -105,3 +112,4 @@ def test_forward_sharded_world2_matches_unsharded(golden):
         np.testing.assert_allclose(r["logits"], ref_logits, rtol=1e-12, atol=1e-12)
         assert abs(float(r["loss"]) - ref_loss) <= 1e-6 * abs(ref_loss)  # combined in fp64, returned fp32
         assert abs(float(r["loss1"]) - ref_loss1) <= 1e-6 * abs(ref_loss1)
+        assert bool(r["raised"])
