@@ -76,6 +76,8 @@ def parse_args():
     ap.add_argument("--vocab", type=int, default=50257)
     ap.add_argument("--qkv-layout", choices=["separate", "packed"], default="separate",
                     help="attention workload: separate [B,T,H,Dh] q/k/v, or views of one [B,T,3,H,Dh] buffer")
+    ap.add_argument("--attn-softmax", choices=["bound", "online"], default="bound",
+                    help="attention workload: nGPT score-bound offset (the forward's call) or running-max softmax")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -456,9 +458,20 @@ def run_attention(a, world, rank, local_rank):
         q, k, v = packed[:, :, 0], packed[:, :, 1], packed[:, :, 2]
     scale = math.sqrt(Dh)
 
+    o_buf = torch.empty(B, T, H, Dh, device=dev, dtype=torch.bfloat16)
+    strides = K.attention_strides(q, k, v, o_buf, head_major=False)
+    s_heads = s.to(dev).expand(H, Dh).contiguous()
+    st = _lib.stream_handle(dev)
+
     def ours():
-        with torch.no_grad():
-            return K.causal_sdpa(q, k, v, scale=scale, dropout_p=0.0, impl="tcgen05")
+        if a.attn_softmax == "bound":
+            # the forward's call: softmax offset from the per-head score bound max s^2
+            _lib.call("engpt_ngpt_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), o_buf.data_ptr(), _lib.BF16,
+                      B, T, H, Dh, float(scale), strides.data_ptr(), s_heads.data_ptr(), 1.0, st)
+        else:
+            _lib.call("engpt_causal_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), o_buf.data_ptr(),
+                      _lib.BF16, B, T, H, Dh, float(scale), strides.data_ptr(), _lib.ATTN_TCGEN05, st)
+        return o_buf
 
     def torch_sdpa():
         return torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
@@ -490,7 +503,8 @@ def run_attention(a, world, rank, local_rank):
         "metric": "isolated nGPT causal attention TFLOP/s", "value": achieved, "unit": "TFLOP/s",
         "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
         "dtype": "bf16", "data": "synthetic (seeded normal q/k/v, unit q/k scaled by U(0.9,1.1))",
-        "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh), q/k/v {a.qkv_layout}",
+        "config": {"workload": f"causal attention B={B} H={H} T={T} Dh={Dh}, scale sqrt(Dh), q/k/v {a.qkv_layout}, "
+                               f"softmax {a.attn_softmax}",
                    "l2": "inputs read once per launch; no flush between launches"},
         "roofline": {"kernel": "attn_fwd2_kernel (tcgen05)" if Dh == 64 else f"attn_fwd_kernel<{Dh}> (tcgen05)", "bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],

@@ -66,7 +66,17 @@ struct Params {
   int B, T, H;
   int n_qt;
   float scale_log2;
+  // nGPT score bound (head_dim 64 kernel): q and k of head h are unit vectors times s_qk[h, :] * s_mult
+  // (the QKV post-process output), so |q.k| <= max_i (s_qk[h, i] s_mult)^2.  nullptr: general inputs.
+  const float* s_qk;
+  float s_mult;
 };
+
+// Largest per-head bound (log2 units) the fixed-offset softmax takes: every exponent x = s * scale * log2(e) - M
+// then lies in [-2M, 0] (a little above 0 for bf16 rounding of q and k), so with M <= 48 the row sums and P stay
+// >= 2^-96, far inside the fp32 / bf16 normal range even after scaling by small v.  A head whose bound is larger
+// runs the running-max softmax.
+constexpr float kStaticBoundMax = 48.0f;
 
 // One CTA owns a 128-query tile of one (batch, head) and walks the causal
 // prefix of 128-key tiles.  Warp roles (192 threads):
@@ -556,6 +566,97 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, ui
   tmem_st16(tP, pw);
 }
 
+// 2^x for a pair of finite x >= -120 on the FMA pipe (Cody-Waite style range reduction and a polynomial), so
+// that part of the exponentials bypasses the MUFU unit: x = n + f with n the nearest integer (the 1.5 * 2^23
+// addition leaves n in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f from a cubic fitted here for
+// relative error on [-0.5, 0.5] (max 7.5e-5, far below the bf16 rounding of P), and 2^n added to its exponent
+// field: bits(t) << 23 == n << 23 modulo 2^32.
+#ifndef ENGPT_ATTN_POLY_PAIRS
+#define ENGPT_ATTN_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = ENGPT_ATTN_POLY_PAIRS;   // pairs of each 16 whose exponentials use the polynomial
+__device__ __forceinline__ bool poly_pair(int i) {   // spread over the chunk: every (16 / kPolyPairs)-th pair
+  return kPolyPairs > 0 && (i * kPolyPairs) % 16 < kPolyPairs;
+}
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& e0, float& e1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t t2 = fadd2(x2, magic);
+  const uint64_t f2 = fsub2(x2, fsub2(t2, magic));
+  uint64_t p2 = ffma2(f2, f2_pack(0.05517167f, 0.05517167f), f2_pack(0.24261114f, 0.24261114f));
+  p2 = ffma2(p2, f2, f2_pack(0.69326097f, 0.69326097f));
+  p2 = ffma2(p2, f2, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(p2, p0, p1);
+  f2_unpack(t2, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Fixed-offset softmax of the 64 scores of this half row in one job: p = 2^(s * sl2 - M) with M the head's
+// score bound, so no running max, no raise and no rescale of P, l or O.  The row sum adds the bf16-rounded P
+// that the PV product multiplies, so the normalisation matches the weights exactly (a row with one dominant
+// key returns that key's v).  Masked keys (after the query) give 0; a 32-key chunk after every query of the
+// warp is written as zeros without exponentiating.
+__device__ __forceinline__ void static_job(uint32_t tS, uint32_t tP0, int kbase, int q_idx, uint64_t sc2,
+                                           uint64_t nm2, bool diag, uint64_t& l2) {
+  uint32_t r[32];
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    uint32_t pw[16];
+    const int key0 = kbase + 32 * cc;
+    tmem_ld32(tS + 32 * cc, r);
+    tmem_wait_ld32(r);
+    if (diag && __all_sync(0xffffffffu, key0 > q_idx)) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pw[i] = 0u;
+    } else {
+      const bool mask = diag && __any_sync(0xffffffffu, key0 + 31 > q_idx);
+      uint64_t ca = f2_pack(0.f, 0.f), cb = f2_pack(0.f, 0.f);
+      if (mask) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0, x1;
+          f2_unpack(ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2), x0, x1);
+          if (key0 + 2 * i > q_idx) x0 = -INFINITY;
+          if (key0 + 2 * i + 1 > q_idx) x1 = -INFINITY;
+          pw[i] = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
+          const uint64_t pr = f2_pack(__uint_as_float(pw[i] << 16), __uint_as_float(pw[i] & 0xffff0000u));
+          if (i & 1) cb = fadd2(cb, pr); else ca = fadd2(ca, pr);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint64_t x2 = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
+          float e0, e1;
+          if (poly_pair(i)) {
+            exp2_poly2(x2, e0, e1);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+          }
+          pw[i] = pack_bf16x2(e0, e1);
+          const uint64_t pr = f2_pack(__uint_as_float(pw[i] << 16), __uint_as_float(pw[i] & 0xffff0000u));
+          if (i & 1) cb = fadd2(cb, pr); else ca = fadd2(ca, pr);
+        }
+      }
+      l2 = fadd2(l2, fadd2(ca, cb));
+    }
+    tmem_st16(tP0 + 16 * cc, pw);
+  }
+}
+
+// Score bound of head h in log2 units: |q.k| <= max_i (s_qk[h,i] s_mult)^2 for q = u * s, k = w * s with unit
+// u, w (|sum u_i w_i s_i^2| <= max s^2 sum |u_i w_i| <= max s^2), times |scale| log2(e); the 1/64 margin covers
+// the bf16 rounding of q and k.  Warp-uniform.
+__device__ __forceinline__ float head_bound_log2(const Params& p, int h, int lane) {
+  const float* s = p.s_qk + (int64_t)h * D;
+  const float a = s[lane] * p.s_mult, b = s[lane + 32] * p.s_mult;
+  const float m = warp_max(fmaxf(a * a, b * b));
+  return fabsf(p.scale_log2) * m * (1.0f + 1.0f / 64.0f);
+}
+
 // Band k of this CTA.  The grid is persistent (one CTA per SM) and takes the bands in rounds of gridDim.x:
 // round k covers the global band indices [k G, k G + G), in snake order (CTA c takes k G + c in even rounds,
 // k G + G - 1 - c in odd ones), which balances the band sizes across CTAs (the heaviest and lightest bands
@@ -875,6 +976,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       st.m = 0.f;
       st.kr = 0.f;
       st.l2 = f2_pack(0.f, 0.f);
+      // the same bound in every warp of the band (same head, same arithmetic): both halves of a row take the
+      // same path, so the online path's pair barriers stay matched
+      const float bound = p.s_qk ? head_bound_log2(p, bi.h, lane) : INFINITY;
+      const bool fixed = bound <= kStaticBoundMax;
+      const uint64_t nm2 = f2_pack(-bound, -bound);
       for (int j = 0; j < n_w; ++j) {
         // A failed (timed-out) wait poisons this warp: it skips the remaining work but still takes every pair
         // barrier below, so the other warp of the pair never waits on a barrier this one skips.
@@ -888,6 +994,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tP0 = tS + 64 * hf;     // this half's P columns (over its first score chunk)
         const int kbase = j * BN + 64 * hf;    // this half's first key
         st.kr = 0.f;
+        if (fixed) {
+          // fixed offset: the head's score bound
+          if (ok) {
+            tc_fence_after();
+            const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
+            static_job(tP0, tP0, kbase, q_idx, f2_pack(sl2, sl2), nm2, diag, st.l2);
+          }
+        } else {
         if (ok) {
           tc_fence_after();
           const bool diag = __any_sync(0xffffffffu, kbase + 63 > q_idx);
@@ -940,6 +1054,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             st.m += k_all;
           }
         }
+        }   // running-max path
         if (ok) {
           tmem_wait_st();
           tc_fence_before();
@@ -1013,7 +1128,7 @@ static bool tc_eligible(const void* q, const void* k, const void* v, void* o, in
 }
 
 static int launch_v2(const void* q, const void* k, const void* v, void* o, int B, int T, int H, float scale,
-                     const int64_t* s, cudaStream_t st) {
+                     const int64_t* s, const float* s_qk, float s_mult, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_map(&mq, q, 64, T, H, B, s[1], s[2], s[0]))) return rc;
@@ -1029,6 +1144,8 @@ static int launch_v2(const void* q, const void* k, const void* v, void* o, int B
   p.H = H;
   p.n_qt = (T + 255) / 256;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.s_qk = s_qk;
+  p.s_mult = s_mult;
   const int64_t bands = (int64_t)p.n_qt * B * H;
   ENGPT_REQUIRE(bands <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
   const int64_t blocks = std::min<int64_t>(bands, num_sms());   // persistent: one CTA per SM
@@ -1058,6 +1175,8 @@ static int launch(const void* q, const void* k, const void* v, void* o, int B, i
   p.H = H;
   p.n_qt = (T + BM - 1) / BM;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.s_qk = nullptr;
+  p.s_mult = 1.0f;
   const int64_t blocks = (int64_t)p.n_qt * B * H;
   ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
   auto kern = attn_fwd_kernel<D>;
@@ -1091,9 +1210,28 @@ extern "C" int engpt_causal_attention(const void* q, const void* k, const void* 
     if (rc) return rc;
     if (Dh == 64) {
       if (impl == ENGPT_ATTN_TCGEN05_1TILE) return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, st);
-      return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, st);
+      return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, nullptr, 1.0f, st);
     }
     return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, st);
   }
   return launch_attn_simt(q, k, v, o, dtype, B, T, H, Dh, scale, strides, st);
+}
+
+extern "C" int engpt_ngpt_attention(const void* q, const void* k, const void* v, void* o, int dtype, int B, int T,
+                                    int H, int Dh, float scale, const int64_t* strides, const float* qk_scale,
+                                    float qk_mult, void* stream) {
+  clear_error();
+  ENGPT_REQUIRE(qk_scale != nullptr, ENGPT_ERR_ARG, "ngpt_attention: null qk_scale");
+  ENGPT_REQUIRE(B >= 0 && T >= 0 && H > 0 && Dh > 0, ENGPT_ERR_SHAPE, "ngpt_attention: B=%d T=%d H=%d Dh=%d", B, T,
+                H, Dh);
+  ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "ngpt_attention: dtype %d", dtype);
+  if ((int64_t)B * T == 0) return ENGPT_OK;
+  ENGPT_REQUIRE(q && k && v && o && strides, ENGPT_ERR_ARG, "ngpt_attention: null pointer");
+  if (dtype == ENGPT_BF16 && Dh == 64 && attn_tc::tc_eligible(q, k, v, o, Dh, strides)) {
+    int rc = attn_tc::get_encode();
+    if (rc) return rc;
+    return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, qk_scale, qk_mult, as_stream(stream));
+  }
+  // other head dims and fp32: the general kernels (their running-max softmax is exact for any scores)
+  return engpt_causal_attention(q, k, v, o, dtype, B, T, H, Dh, scale, strides, ENGPT_ATTN_AUTO, stream);
 }

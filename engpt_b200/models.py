@@ -370,9 +370,16 @@ class EfficientNGPT(nn.Module):
                               _lib.QKV_INPLACE, st)
                 if self.attn_timer is not None:
                     self.attn_timer("start")
-                _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
-                          ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
-                          self.attn_impl, st)
+                if self.attn_impl == _lib.ATTN_AUTO:
+                    # q, k are unit vectors times the effective s_qk (the post-process above): the kernel takes
+                    # its softmax offset from the per-head score bound max_i s_qk[h, i]^2 (no running max)
+                    _lib.call("engpt_ngpt_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
+                              ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
+                              blk.s_qk.data_ptr(), float(blk.qk_mult), st)
+                else:
+                    _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
+                              ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
+                              self.attn_impl, st)
                 if self.attn_timer is not None:
                     self.attn_timer("stop")
                 fuse_res = bf16 and self.fuse_residual and d % 256 == 0 and d <= 1024

@@ -180,12 +180,13 @@ def test_attention_tcgen05_bf16_vs_oracle(cuda, D, T):
     assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
 
 
-@pytest.mark.parametrize("B,T,H", [(8, 1152, 16), (2, 2048, 16)])
+@pytest.mark.parametrize("B,T,H", [(8, 1152, 16), (8, 1200, 16), (2, 2048, 16)])
 def test_attention_tcgen05_many_bands_per_cta(cuda, B, T, H):
     """More 256-query bands than SMs, so every CTA of the persistent head_dim-64 kernel walks several bands:
     the Q double buffer, the job / K-V / PV counters that run across bands, the band store deferred past the
-    next band's first job, and (T = 1152) last bands whose second 128-row tile is empty.  Reference: torch's
-    fp32 causal SDPA on the same bf16-rounded inputs; bound as in the oracle test above."""
+    next band's first job, last bands whose second 128-row tile is empty (T = 1152: T mod 256 = 128) or only
+    partly filled (T = 1200: T mod 256 = 176).  Reference: torch's fp32 causal SDPA on the same bf16-rounded
+    inputs; bound as in the oracle test above."""
     D = 64
     q, k, v = _attn_inputs(B, T, H, D, seed=B * T + H)
     qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
@@ -201,6 +202,81 @@ def test_attention_tcgen05_many_bands_per_cta(cuda, B, T, H):
     err_torch = (sdpa(qb, kb, vb).float() - ref).abs().max().item()
     assert err < 1.5e-2, (err, err_torch)
     assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
+
+
+def _ngpt_inputs(B, T, H, D, s_heads, seed):
+    """Unit q/k per head times an effective scale s[h, :] (the QKV post-process output), v ~ N(0, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(B, T, H, D, generator=g) for _ in range(3))
+    s = torch.stack([torch.rand(D, generator=g) * 0.2 + (sh - 0.1) for sh in s_heads])    # [H, D]
+    q = q / q.norm(dim=-1, keepdim=True) * s
+    k = k / k.norm(dim=-1, keepdim=True) * s
+    return q, k, v, s
+
+
+def _ngpt_attention(cuda, qb, kb, vb, s_raw, mult, scale):
+    B, T, H, D = qb.shape
+    o = torch.empty_like(qb)
+    strides = K.attention_strides(qb, kb, vb, o, head_major=False)
+    s_dev = s_raw.to(cuda, torch.float32).contiguous()
+    _lib.call("engpt_ngpt_attention", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), o.data_ptr(), _lib.BF16, B, T, H,
+              D, float(scale), strides.data_ptr(), s_dev.data_ptr(), float(mult), _stream())
+    return o
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 1, 3), (2, 100, 3), (2, 128, 3), (1, 130, 2), (2, 333, 3), (2, 1024, 4),
+                                   (8, 1200, 16), (4, 2048, 16)])
+def test_ngpt_attention_fixed_offset_vs_oracle(cuda, B, T, H):
+    """Head_dim-64 kernel with the softmax offset taken from the per-head score bound (no running max), against
+    the fp64 oracle on the same bf16 inputs: within torch's own bf16 SDPA error, as the general kernel."""
+    D = 64
+    q, k, v, s = _ngpt_inputs(B, T, H, D, [1.0] * H, seed=B * T + H)
+    qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
+    o = _ngpt_attention(cuda, qb, kb, vb, s / 32.0, 32.0, 8.0)       # raw parameter x multiplier
+    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), 8.0)
+    err = np.abs(o.float().cpu().numpy() - ref).max()
+    sd = torch.nn.functional.scaled_dot_product_attention(qb.transpose(1, 2), kb.transpose(1, 2),
+                                                          vb.transpose(1, 2), is_causal=True,
+                                                          scale=8.0).transpose(1, 2)
+    err_torch = np.abs(sd.float().cpu().numpy() - ref).max()
+    assert err < 1.5e-2, (err, err_torch)
+    assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
+
+
+def test_ngpt_attention_mixed_heads_take_both_softmax_paths(cuda):
+    """Heads whose bound is small (fixed offset) and large (s = 3: 8 log2(e) 9 > 48, running max) in one launch,
+    several bands per CTA: both paths against the oracle, per head within twice torch's own bf16 SDPA error (the
+    s = 3 heads are nearly one-hot, where bf16 rounding of the inputs dominates)."""
+    B, T, H, D = 4, 1536, 8, 64
+    q, k, v, s = _ngpt_inputs(B, T, H, D, [1.0, 3.0, 0.5, 1.0, 3.0, 1.0, 2.2, 1.0], seed=17)
+    qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
+    o = _ngpt_attention(cuda, qb, kb, vb, s, 1.0, 8.0)
+    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), 8.0)
+    sd = torch.nn.functional.scaled_dot_product_attention(qb.transpose(1, 2), kb.transpose(1, 2),
+                                                          vb.transpose(1, 2), is_causal=True,
+                                                          scale=8.0).transpose(1, 2).float().cpu().numpy()
+    got = o.float().cpu().numpy()
+    for h in range(H):
+        err = np.abs(got[:, :, h] - ref[:, :, h]).max()
+        err_torch = np.abs(sd[:, :, h] - ref[:, :, h]).max()
+        assert err <= 2.0 * err_torch + 2e-3, (h, err, err_torch)
+
+
+def test_ngpt_attention_isolated_cfg2(golden, cuda):
+    """The isolated attention configuration (B=8, H=16, T=2048, Dh=64, s ~ U(0.9, 1.1)) through the fixed-offset
+    kernel against the reference's golden rows."""
+    g = golden("attn_cfg2.npz")
+    B, H, T, D = 8, 16, 2048, 64
+    gen = torch.Generator().manual_seed(1)
+    q, k, v = (torch.randn(B, T, H, D, generator=gen) for _ in range(3))
+    s = torch.rand(D, generator=gen) * 0.2 + 0.9
+    q = q / q.norm(dim=-1, keepdim=True) * s
+    k = k / k.norm(dim=-1, keepdim=True) * s
+    o = _ngpt_attention(cuda, *(x.to(cuda, torch.bfloat16) for x in (q, k, v)), s.expand(H, D), 1.0, 8.0)
+    rows = g["rows"]
+    np.testing.assert_allclose(o[0, rows].float().cpu().numpy(), g["o_b0_rows"], atol=1.5e-2)
+    np.testing.assert_allclose(o[7, rows].float().cpu().numpy(), g["o_b7_rows"], atol=1.5e-2)
+    assert abs(o.double().abs().sum().item() - float(g["o_abs_sum"])) / float(g["o_abs_sum"]) < 5e-3
 
 
 @pytest.mark.parametrize("D", [64, 128])
@@ -395,6 +471,42 @@ def test_qkv_projection_matches_unfused_path(cuda, B, T):
               Dh // 2, qks.data_ptr(), 2.0, 1e-6, B, T, H, Dh, None, None, None, _lib.QKV_INPLACE, _stream())
     diff = (fused.float() - unf.float()).abs().max().item()
     assert diff <= 2e-2 * unf.float().abs().max().item(), diff
+
+
+@pytest.mark.parametrize("B,T", [(2, 2048), (1, 300)])
+def test_qkv_projection_vs_oracle_d1024(cuda, B, T):
+    """Fused QKV GEMM + post-process at the benchmarked width (d=1024, H=16, Dh=64) against the fp64 oracle
+    (engpt/kernels.py:139-179 on the exact product of the bf16 operands): every q/k/v row within bf16 output
+    rounding, 8e-3 of its norm."""
+    H, Dh = 16, 64
+    d = H * Dh
+    n = B * T
+    g = torch.Generator().manual_seed(B * T)
+    x = torch.nn.functional.normalize(torch.randn(n, d, generator=g), dim=-1).to(cuda, torch.bfloat16)
+    w = torch.nn.functional.normalize(torch.randn(3 * d, d, generator=g), dim=-1).to(cuda, torch.bfloat16)
+    rho = (torch.rand(n, generator=g) * 40 + 0.5).to(cuda)
+    cos, sin = K.rotary_frequencies(T, Dh, device=cuda, dtype=torch.float32, theta=10000.0)
+    s_qk = (torch.rand(H, Dh, generator=g) * 0.2 + 0.9) / 32.0      # raw parameter; x 32 = effective
+    s_qk = s_qk.to(cuda)
+    out = torch.empty(n, 3 * d, device=cuda, dtype=torch.bfloat16)
+    _lib.call("engpt_qkv_projection", x.data_ptr(), w.data_ptr(), rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+              Dh // 2, s_qk.data_ptr(), 32.0, 1e-6, B, T, H, Dh, out.data_ptr(), _stream())
+    x64 = x.double().cpu().numpy()
+    w64 = w.double().cpu().numpy()
+    raw = (x64 @ w64.T).reshape(B, T, 3, H, Dh)
+    eff = (s_qk.cpu() * 32.0).numpy().astype(np.float64)
+    ref = O.qkv_postprocess_from_carried(raw, rho.cpu().numpy().astype(np.float64).reshape(B, T),
+                                         cos.cpu().numpy().astype(np.float64), sin.cpu().numpy().astype(np.float64),
+                                         eff, 1e-6)
+    got = out.float().cpu().numpy().reshape(B, T, 3, H, Dh)
+    for i in range(3):
+        err = row_rel(got[:, :, i].reshape(-1, Dh), ref[i].reshape(-1, Dh))
+        assert err < 8e-3, (i, err)
+
+
+def row_rel(a, b):
+    num = np.sqrt(((np.asarray(a, np.float64) - b) ** 2).sum(-1))
+    return float((num / np.maximum(np.sqrt((b ** 2).sum(-1)), 1e-30)).max())
 
 
 def _residual_case(cuda, rows, d, K, seed):
