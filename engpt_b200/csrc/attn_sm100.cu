@@ -566,32 +566,6 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t* r, uint32_t tP, ui
   tmem_st16(tP, pw);
 }
 
-// 2^x for a pair of finite x >= -120 on the FMA pipe (Cody-Waite style range reduction and a polynomial), so
-// that part of the exponentials bypasses the MUFU unit: x = n + f with n the nearest integer (the 1.5 * 2^23
-// addition leaves n in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f from a cubic fitted here for
-// relative error on [-0.5, 0.5] (max 7.5e-5, far below the bf16 rounding of P), and 2^n added to its exponent
-// field: bits(t) << 23 == n << 23 modulo 2^32.
-#ifndef ENGPT_ATTN_POLY_PAIRS
-#define ENGPT_ATTN_POLY_PAIRS 0
-#endif
-constexpr int kPolyPairs = ENGPT_ATTN_POLY_PAIRS;   // pairs of each 16 whose exponentials use the polynomial
-__device__ __forceinline__ bool poly_pair(int i) {   // spread over the chunk: every (16 / kPolyPairs)-th pair
-  return kPolyPairs > 0 && (i * kPolyPairs) % 16 < kPolyPairs;
-}
-__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& e0, float& e1) {
-  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t t2 = fadd2(x2, magic);
-  const uint64_t f2 = fsub2(x2, fsub2(t2, magic));
-  uint64_t p2 = ffma2(f2, f2_pack(0.05517167f, 0.05517167f), f2_pack(0.24261114f, 0.24261114f));
-  p2 = ffma2(p2, f2, f2_pack(0.69326097f, 0.69326097f));
-  p2 = ffma2(p2, f2, f2_pack(0.99992806f, 0.99992806f));
-  float p0, p1, t0, t1;
-  f2_unpack(p2, p0, p1);
-  f2_unpack(t2, t0, t1);
-  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-}
-
 // Fixed-offset softmax of the 64 scores of this half row in one job: p = 2^(s * sl2 - M) with M the head's
 // score bound, so no running max, no raise and no rescale of P, l or O.  The row sum adds the bf16-rounded P
 // that the PV product multiplies, so the normalisation matches the weights exactly (a row with one dominant
@@ -612,34 +586,20 @@ __device__ __forceinline__ void static_job(uint32_t tS, uint32_t tP0, int kbase,
     } else {
       const bool mask = diag && __any_sync(0xffffffffu, key0 + 31 > q_idx);
       uint64_t ca = f2_pack(0.f, 0.f), cb = f2_pack(0.f, 0.f);
-      if (mask) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0, x1;
-          f2_unpack(ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2), x0, x1);
+      for (int i = 0; i < 16; ++i) {
+        float x0, x1;
+        f2_unpack(ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2), x0, x1);
+        if (mask) {
           if (key0 + 2 * i > q_idx) x0 = -INFINITY;
           if (key0 + 2 * i + 1 > q_idx) x1 = -INFINITY;
-          pw[i] = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
-          const uint64_t pr = f2_pack(__uint_as_float(pw[i] << 16), __uint_as_float(pw[i] & 0xffff0000u));
-          if (i & 1) cb = fadd2(cb, pr); else ca = fadd2(ca, pr);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint64_t x2 = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
-          float e0, e1;
-          if (poly_pair(i)) {
-            exp2_poly2(x2, e0, e1);
-          } else {
-            float x0, x1;
-            f2_unpack(x2, x0, x1);
-            e0 = ex2_approx(x0);
-            e1 = ex2_approx(x1);
-          }
-          pw[i] = pack_bf16x2(e0, e1);
-          const uint64_t pr = f2_pack(__uint_as_float(pw[i] << 16), __uint_as_float(pw[i] & 0xffff0000u));
-          if (i & 1) cb = fadd2(cb, pr); else ca = fadd2(ca, pr);
-        }
+        pw[i] = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
+        const uint64_t pr = f2_pack(__uint_as_float(pw[i] << 16), __uint_as_float(pw[i] & 0xffff0000u));
+        if (i & 1)
+          cb = fadd2(cb, pr);
+        else
+          ca = fadd2(ca, pr);
       }
       l2 = fadd2(l2, fadd2(ca, cb));
     }
@@ -727,6 +687,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // bounded wait taken by a whole converged warp (the issuer warps), with a warp-uniform result
+  auto wwait = [&](uint32_t b, uint32_t parity, int site) -> bool {
+    return __all_sync(0xffffffffu, mbar_wait(b, parity, abort_flag, site));
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -815,11 +779,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpS) {
     // ------------------------------------------------------------ S issuer
-    // One thread walks the job stream over all of this CTA's bands and issues S(G) = Q K_j^T into slot G % 3
+    // The warp walks the job stream (MMAs and commits from one elected lane) over all of this CTA's bands and issues S(G) = Q K_j^T into slot G % 3
     // once the PV that read P(G - 3) from that slot completed.  The S and PV issuers are separate threads, so neither's
     // waits and issue latency delay the other; tcgen05 MMAs of different threads are unordered, which is
     // fine: S and PV share no accumulator, and every hand-off between them goes through the softmax.
-    if (lane == 0) {
+    {
       constexpr uint32_t kIdescS = idesc_bf16_f32(128, BN, false, false);
       const uint64_t dk0 = sw128_desc(sbase + L::K, 16, 1024);
       int k_waited = -1;   // K tiles up to this one are known loaded (the jobs' tiles never go back)
@@ -831,12 +795,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int G = cs.jbase + cs.g;
         const int slot = G % NSLOT;
         // PV(G - 3) completed; the slot's next PFREE phase needs PV(G), which needs S(G), issued below
-        if (G >= NSLOT && !mbar_wait(bar(B_PFREE + slot), ((G / NSLOT) - 1) & 1, abort_flag, 26)) break;
-        if (cs.g == 0 && !mbar_wait(bar(B_Q + (cs.k & 1)), (cs.k >> 1) & 1, abort_flag, 22)) break;
+        if (G >= NSLOT && !wwait(bar(B_PFREE + slot), ((G / NSLOT) - 1) & 1, 26)) break;
+        if (cs.g == 0 && !wwait(bar(B_Q + (cs.k & 1)), (cs.k >> 1) & 1, 22)) break;
         const int kvg = cs.kvbase + j;
         const int s = kvg % NS;
         if (kvg > k_waited) {
-          if (!mbar_wait(bar(B_KFULL + s), (kvg / NS) & 1, abort_flag, 23)) break;
+          if (!wwait(bar(B_KFULL + s), (kvg / NS) & 1, 23)) break;
           k_waited = kvg;
         }
         tc_fence_after();
@@ -844,21 +808,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t db = desc_add(dk0, s * kBlockBytes);
         const uint32_t td = tmem + 128 * slot;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) umma_f16_ss(td, da + 2 * kk, db + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
-        umma_commit(bar(B_SFULL + NSLOT * w + slot));
-        if (cs.bi.bd.nB == 0 || w == 1) umma_commit(bar(B_KEMPTY + s));          // last S that reads K_j
-        if (cs.g == cs.bi.n_jobs - 1) umma_commit(bar(B_QFREE + (cs.k & 1)));   // the band's last S
+        for (int kk = 0; kk < D / 16; ++kk) umma_f16_ss_w(td, da + 2 * kk, db + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
+        umma_commit_w(bar(B_SFULL + NSLOT * w + slot));
+        if (cs.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_KEMPTY + s));          // last S that reads K_j
+        if (cs.g == cs.bi.n_jobs - 1) umma_commit_w(bar(B_QFREE + (cs.k & 1)));   // the band's last S
         cs.next(p);
       }
-      umma_commit(bar(B_FINAL));
+      umma_commit_w(bar(B_FINAL));
       volatile int never = 0;
       mbar_wait(bar(B_FINAL), 0, &never, 27);
     }
     __syncwarp();
   } else if (warp == kWarpPV) {
     // ------------------------------------------------------------ PV issuer
-    // One thread issues O_tile += P(G) V_j for each job G once the softmax wrote P(G).
-    if (lane == 0) {
+    // The warp issues O_tile += P(G) V_j for each job G once the softmax wrote P(G).
+    {
       constexpr uint32_t kIdescPV = idesc_bf16_f32(128, D, false, true);
       const uint64_t dv0 = sw128_desc(sbase + L::V, kBlockBytes, 1024);
       int v_waited = -1;
@@ -873,15 +837,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kvg = cp.kvbase + j;
         const int s = kvg % NS;
         if (kvg > v_waited) {
-          if (!mbar_wait(bar(B_VFULL + s), (kvg / NS) & 1, abort_flag, 35)) break;
+          if (!wwait(bar(B_VFULL + s), (kvg / NS) & 1, 35)) break;
           v_waited = kvg;
         }
         // P(G) written; the slot's next TDONE phase needs S(G + 3), which waits for this PV
-        if (!mbar_wait(bar(B_TDONE + slot), (G / NSLOT) & 1, abort_flag, 24)) break;
+        if (!wwait(bar(B_TDONE + slot), (G / NSLOT) & 1, 24)) break;
         if (j == 0) {
           // this PV starts the tile's O afresh: the softmax loaded O of the tile's previous band.  The next
           // OREAD phase of the tile needs this band's PVs, so the parity wait is unambiguous.
-          if (bands_w[w] > 0 && !mbar_wait(bar(B_OREAD + w), (bands_w[w] - 1) & 1, abort_flag, 36)) break;
+          if (bands_w[w] > 0 && !wwait(bar(B_OREAD + w), (bands_w[w] - 1) & 1, 36)) break;
           ++bands_w[w];
         }
         tc_fence_after();
@@ -891,14 +855,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // keys 16kk..16kk+15: P columns p_col(8kk) of the slot, V rows 16kk.. (2048 bytes apart)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16_ts(td, ta + p_col(8 * kk), db + 128 * kk, kIdescPV, (kk > 0 || j > 0) ? 1u : 0u);
+          umma_f16_ts_w(td, ta + p_col(8 * kk), db + 128 * kk, kIdescPV, (kk > 0 || j > 0) ? 1u : 0u);
         const int pv = cp.pvbase[w] + j;       // this tile's pv-th PV
-        umma_commit(bar(B_ODONE + 2 * w + (pv & 1)));
-        umma_commit(bar(B_PFREE + slot));
-        if (cp.bi.bd.nB == 0 || w == 1) umma_commit(bar(B_VEMPTY + s));          // last PV that reads V_j
+        umma_commit_w(bar(B_ODONE + 2 * w + (pv & 1)));
+        umma_commit_w(bar(B_PFREE + slot));
+        if (cp.bi.bd.nB == 0 || w == 1) umma_commit_w(bar(B_VEMPTY + s));          // last PV that reads V_j
         cp.next(p);
       }
-      umma_commit(bar(B_FINAL));
+      umma_commit_w(bar(B_FINAL));
     }
     __syncwarp();
   } else {
@@ -1091,6 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace v2
 
 
+
 // --------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -1150,9 +1115,10 @@ static int launch_v2(const void* q, const void* k, const void* v, void* o, int B
   ENGPT_REQUIRE(bands <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
   const int64_t blocks = std::min<int64_t>(bands, num_sms());   // persistent: one CTA per SM
   auto kern = v2::attn_fwd2_kernel;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, v2::Layout::kDynSmem);
+  const int threads = v2::kThreads, smem = v2::Layout::kDynSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return set_error(ENGPT_ERR_LAUNCH, "attention: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<(unsigned)blocks, v2::kThreads, v2::Layout::kDynSmem, st>>>(mq, mk, mv, p);
+  kern<<<(unsigned)blocks, threads, smem, st>>>(mq, mk, mv, p);
   return check_launch("attention (tcgen05, 2-tile)");
 }
 
