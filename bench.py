@@ -1,11 +1,14 @@
 """Forward-throughput benchmark of the enGPT hot path on B200.
 
 Workload (one "step"): ``EfficientNGPT`` forward + token cross-entropy under
-bf16 autocast, L=16, d=1024, H=16 (head_dim 64), T=2048, vocab 50257, batch
-32 sequences per GPU, random-init unit-sphere weights (seed 0) and uniform
-random token ids (synthetic data).  Multi-GPU runs are weak-scaled: each rank
-runs its own 32-sequence shard (batch split, no collective inside the hot
-path); one NCCL all-reduce of the scalar loss per step gathers the result.
+bf16 autocast, L=16, d=1024, H=16 (head_dim 64), T=2048, vocab 50257, a
+global batch of 32 sequences, random-init unit-sphere weights (seed 0) and
+uniform random token ids (synthetic data).  With N GPUs (one process each)
+the batch is split by sequences over the ranks (strong scaling: 4 sequences
+per GPU at N=8), with no collective inside the forward; each step ends with
+one NCCL all-reduce of the token-weighted loss and an all-gather of every
+shard's final represented state Y/rho (``--gather``).  ``--scaling weak``
+runs ``--batch`` sequences per rank instead.
 
 Reported (one JSON line from rank 0):
   value      tokens/s over all ranks, inputs resident in HBM, device-timed
@@ -14,7 +17,9 @@ Reported (one JSON line from rank 0):
              with pinned host ids/targets copied in and the loss copied out
              inside the timed region
   roofline   the attention kernel (tcgen05) against bf16 tensor peak
-  kernels    per-kernel averages of the other CUDA kernels (HBM roofline)
+  kernels    per-kernel averages of the CUDA kernels of one forward
+  reference_gpu  the reference package's own eager GPU forward at this
+             workload and at the shape of its published numbers (N=1)
   cpu_baseline  the oracle's fp32 numpy forward on the host cores (N=1 only)
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
@@ -32,6 +37,18 @@ import subprocess
 import sys
 import tempfile
 import time
+
+
+def _reference_arm(argv):
+    return "--impl=reference" in argv or any(x == "--impl" and argv[i + 1:i + 2] == ["reference"]
+                                              for i, x in enumerate(argv))
+
+
+if _reference_arm(sys.argv):
+    # the CPU reference arm uses every host core: set the BLAS / OpenMP pools before numpy loads them
+    # (torchrun exports OMP_NUM_THREADS=1 to every rank)
+    for _var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_var] = str(os.cpu_count() or 1)
 
 import numpy as np
 
@@ -78,19 +95,29 @@ def parse_args():
                     help="attention workload: separate [B,T,H,Dh] q/k/v, or views of one [B,T,3,H,Dh] buffer")
     ap.add_argument("--attn-softmax", choices=["bound", "online"], default="bound",
                     help="attention workload: nGPT score-bound offset (the forward's call) or running-max softmax")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: --batch sequences in total, split over the ranks; weak: --batch per rank")
+    ap.add_argument("--gather", choices=["hidden", "logits", "none"], default="hidden",
+                    help="N>1: outputs all-gathered over NCCL inside the timed step (final Y/rho, or the logits)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference package's own GPU forward (N=1)")
     return ap.parse_args()
 
 
 def workload_config(a, world):
+    gb = a.batch if a.scaling == "strong" else a.batch * world
     return {
         "workload": (f"EfficientNGPT forward + cross-entropy, bf16 autocast, L={a.layers} d={a.dim} H={a.heads} "
-                     f"T={a.seq} V={a.vocab}, {a.batch} sequences per GPU"),
-        "global_batch": a.batch * world,
+                     f"T={a.seq} V={a.vocab}, {gb} sequences in total"),
+        "global_batch": gb,
         "seq_len": a.seq,
-        "parallelism": f"dp{world} (batch shard per GPU, no collective in the hot path)",
-        "l2": "no flush: activations per step (~10 GB) exceed the 126 MB L2",
+        "parallelism": (f"dp{world}: the batch split by sequences over the ranks ({a.scaling} scaling), no "
+                        f"collective inside the forward"
+                        + (f"; per step one all-reduce of the loss and an all-gather of the {a.gather} outputs"
+                           if world > 1 and a.gather != "none" else "")),
+        "l2": "no flush: activations per step (~10 GB at 32 sequences) exceed the 126 MB L2",
     }
 
 
@@ -110,15 +137,16 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def load_traffic():
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if any."""
+def load_traffic(local_batch=32):
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary (captured at 32 sequences),
+    scaled to this launch's sequences (the traffic is q/k/v/o, proportional to them)."""
     path = os.path.join(ROOT, "profiles", "attn_fwd2_B32_H16_T2048_D64.md")
     if not os.path.exists(path):
         return None
     for line in open(path):
         if line.startswith("traffic_bytes_per_launch:"):
             try:
-                return float(line.split(":", 1)[1].split()[0])
+                return float(line.split(":", 1)[1].split()[0]) * local_batch / 32.0
             except ValueError:
                 return None
     return None
@@ -196,7 +224,20 @@ def cpu_baseline(a, n_seqs):
     return n_seqs * a.seq / dt, dt, loss
 
 
+def _blas_threads():
+    """Threads of the BLAS pool numpy uses (what the CPU legs actually ran with)."""
+    try:
+        from threadpoolctl import threadpool_info
+        n = [p.get("num_threads") for p in threadpool_info() if p.get("user_api") == "blas"]
+        return max(n) if n else None
+    except Exception:  # pragma: no cover - threadpoolctl missing
+        return None
+
+
 def run_reference(a, world, rank):
+    """The reference arm: the oracle port of the reference forward (numpy fp32) on the host cores, rank 0 only.
+
+    It times bounded samples of the workload: --cpu-sample-seqs sequences of --seq tokens per step."""
     if rank != 0:
         return
     import torch
@@ -223,12 +264,14 @@ def run_reference(a, world, rank):
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = a.steps * n * a.seq / total
-    sample = f"{n} x {a.seq}-token sequence(s) of the workload per step, fp32 numpy, {cores} threads"
+    threads = _blas_threads() or cores
+    sample = f"{n} x {a.seq}-token sequence(s) of the workload per step, fp32 numpy, {threads} BLAS threads"
     emit({
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": 1000.0 * total / a.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(a, world),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "warmup": a.warmup, "ms_per_step": 1000.0 * total / a.steps, "higher_is_better": True,
+        "scaling": a.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(a, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
 
@@ -250,10 +293,17 @@ def run_gpu(a, world, rank, local_rank):
     cfg = model_config(a)
     torch.manual_seed(0)
     model = EfficientNGPT(cfg).to(dev).eval().requires_grad_(False)
-    gen = torch.Generator().manual_seed(1000 + rank)
-    idx_h = torch.randint(0, cfg.vocab_size, (a.batch, a.seq), generator=gen)
+    # the global batch: `batch` sequences split over the ranks (strong scaling), or `batch` per rank (weak)
+    global_batch = a.batch if a.scaling == "strong" else a.batch * world
+    gen = torch.Generator().manual_seed(1000)
+    idx_all = torch.randint(0, cfg.vocab_size, (global_batch, a.seq), generator=gen)
+    lo, hi = sharding.shard_range(global_batch, rank, world)
+    if hi - lo == 0:
+        raise SystemExit(f"rank {rank}: no sequences (global batch {global_batch} < {world} ranks)")
+    idx_h = idx_all[lo:hi].contiguous()
     tgt_h = torch.roll(idx_h, -1, dims=1)
     idx_d, tgt_d = idx_h.to(dev), tgt_h.to(dev)
+    local_batch = hi - lo
 
     # count our kernel launches through the C-ABI
     counter = {"n": 0}
@@ -270,9 +320,16 @@ def run_gpu(a, world, rank, local_rank):
     def step(idx, tgt):
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             logits, loss = model(idx, tgt)
-        if world > 1:  # token-weighted mean over all shards: one NCCL all-reduce of 2 doubles
+        out = None
+        if world > 1:
+            # token-weighted mean over all shards (one all-reduce of 2 doubles), then the outputs of every
+            # shard gathered over NCCL: the final represented state [B, T, d] bf16, or the logits
             loss = sharding.combine_loss(loss, n_valid)
-        return logits, loss
+            if a.gather == "hidden":
+                out = sharding.gather_rows(model.last_hidden(), global_batch)
+            elif a.gather == "logits":
+                out = sharding.gather_rows(logits, global_batch)
+        return out, loss
 
     for _ in range(max(a.warmup, 1)):
         step(idx_d, tgt_d)
@@ -298,8 +355,8 @@ def run_gpu(a, world, rank, local_rank):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(a.steps):
-        logits, loss = step(idx_d, tgt_d)
-        del logits
+        out, loss = step(idx_d, tgt_d)
+        del out
     ev1.record()
     torch.cuda.synchronize()
     launches = counter["n"]
@@ -328,44 +385,54 @@ def run_gpu(a, world, rank, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
-    # per-kernel averages of the HBM-bound kernels (one instrumented forward, outside the timed region)
-    kern = profile_kernels(model, step, idx_d, tgt_d, cfg, a)
+    # per-kernel averages of the CUDA kernels (one instrumented forward, outside the timed region)
+    kern = profile_kernels(model, step, idx_d, tgt_d, cfg, a, local_batch)
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, attn_avg], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, attn_avg = t.tolist()
 
+    ref_gpu = None
+    if world == 1 and not a.no_reference_gpu:
+        try:
+            ref_gpu = reference_gpu_timing(a, dev, model)
+        except Exception as exc:  # pragma: no cover - reported, not fatal
+            ref_gpu = {"error": repr(exc)}
+
     if rank != 0:
         return
-    tokens = a.batch * a.seq * world * a.steps
+    tokens = global_batch * a.seq * a.steps
     value = tokens / (ms / 1000.0)
     e2e = tokens / (e2e_ms / 1000.0)
     peaks = load_peaks()
     Dh = a.dim // a.heads
-    attn_flops = 2.0 * a.batch * a.heads * a.seq * a.seq * Dh  # causal: QK^T and PV over the lower triangle
+    attn_flops = 2.0 * local_batch * a.heads * a.seq * a.seq * Dh  # causal: QK^T and PV over the lower triangle
     achieved = attn_flops / (attn_avg / 1000.0) / 1e12
     peak = peaks["bf16_tflops_sustained"]
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform random ids, seeded random-init unit-sphere weights)",
         "config": workload_config(a, world),
-        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * idx_h.numel() * idx_h.element_size() * world,
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * global_batch * a.seq * idx_h.element_size(),
                 "d2h_bytes_per_step": 4 * world},
         "gpu_launches": launches,
         "roofline": {"kernel": "attn_fwd2_kernel (tcgen05, head_dim 64)", "bound": "tensor", "achieved": achieved,
-                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(),
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(local_batch),
                      "peak_source": f"{peaks['source']} bf16 sustained",
                      "avg_launch_ms": attn_avg, "flops_per_launch": attn_flops},
         "kernels": kern,
         "loss": loss_val,
         "clocks": clocks,
     }
+    if ref_gpu is not None:
+        out["reference_gpu"] = ref_gpu
     if world == 1 and not a.no_cpu_baseline:
         try:
             tps, dt, _ = cpu_baseline(a, a.cpu_sample_seqs)
-            out["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+            out["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": _blas_threads() or os.cpu_count() or 1,
+                                   "kind": "port",
                                    "sample": f"{a.cpu_sample_seqs} x {a.seq}-token sequence(s), fp32 numpy oracle, "
                                              f"{dt:.1f} s"}
         except Exception as exc:  # pragma: no cover - reported, not fatal
@@ -373,7 +440,85 @@ def run_gpu(a, world, rank, local_rank):
     emit(out)
 
 
-def profile_kernels(model, step, idx, tgt, cfg, a):
+def _reference_package():
+    """The reference package installed from its sources under baseline/_ref (git-ignored), or None."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "engpt")):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    import engpt
+    return engpt
+
+
+def _time_forward(fn, warmup, steps):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def reference_gpu_timing(a, dev, model):
+    """The reference's own GPU forward beside this one (reported, not the reference arm).
+
+    The reference package's ``EfficientNGPT.forward`` in eager PyTorch under bf16
+    autocast and ``torch.no_grad`` (its benchmark flow, scripts/gpu_train_benchmark.py:148-175),
+    on the same seeded weights and ids: at this workload, and at the shape of its
+    published numbers (L=4, d=256, H=4, T=256, 16 sequences) next to this
+    engine at that shape.
+    """
+    import torch
+    from engpt_b200 import EfficientNGPT, ModelConfig
+    engpt = _reference_package()
+    if engpt is None:
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    out = {"how": "reference engpt.EfficientNGPT.forward, eager PyTorch, bf16 autocast, no_grad, CUDA events"}
+
+    def ref_tokps(cfg_kw, batch, seq, ours=None):
+        torch.manual_seed(0)
+        ref = engpt.EfficientNGPT(engpt.ModelConfig(**cfg_kw)).to(dev).eval()
+        gen = torch.Generator().manual_seed(1000)
+        idx = torch.randint(0, cfg_kw["vocab_size"], (batch, seq), generator=gen).to(dev)
+        tgt = torch.roll(idx, -1, dims=1)
+
+        def run_ref():
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                ref(idx, tgt)
+
+        ms_ref = _time_forward(run_ref, 2, 3)
+        rec = {"reference_tok_s": batch * seq / (ms_ref / 1000.0), "reference_ms": ms_ref}
+        del ref
+        if ours is not None:
+            def run_ours():
+                with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                    ours(idx, tgt)
+            ms = _time_forward(run_ours, 3, 5)
+            rec.update({"engpt_b200_tok_s": batch * seq / (ms / 1000.0), "engpt_b200_ms": ms})
+        torch.cuda.empty_cache()
+        return rec
+
+    cfg_kw = dict(vocab_size=a.vocab, block_size=a.seq, n_layer=a.layers, n_head=a.heads, n_embd=a.dim,
+                  mlp_ratio=4.0, dropout=0.0)
+    out["workload"] = ref_tokps(cfg_kw, a.batch, a.seq)
+    out["workload"]["shape"] = f"L={a.layers} d={a.dim} H={a.heads} T={a.seq}, {a.batch} sequences"
+    pub_kw = dict(vocab_size=50257, block_size=256, n_layer=4, n_head=4, n_embd=256, mlp_ratio=4.0, dropout=0.0)
+    torch.manual_seed(0)
+    small = EfficientNGPT(ModelConfig(**pub_kw)).to(dev).eval().requires_grad_(False)
+    out["published_shape"] = ref_tokps(pub_kw, 16, 256, ours=small)
+    out["published_shape"].update({"shape": "L=4 d=256 H=4 T=256, 16 sequences",
+                                   "published_reference_eager_tok_s": 1247759,
+                                   "published_reference_compiled_tok_s": 2818401})
+    return out
+
+
+def profile_kernels(model, step, idx, tgt, cfg, a, local_batch):
     """Average device time per launch of each C-ABI entry point over one forward (events around each call)."""
     import torch
     from engpt_b200 import _lib
@@ -396,7 +541,7 @@ def profile_kernels(model, step, idx, tgt, cfg, a):
         torch.cuda.synchronize()
     finally:
         _lib.call = real
-    n = a.batch * a.seq
+    n = local_batch * a.seq
     d = a.dim
     peaks = load_peaks()
     # algorithmic bytes per launch (dtypes as used by the engine)

@@ -18,23 +18,33 @@ HOT_PATH_OPS = ("qkv_postprocess_from_carried", "causal_sdpa", "carried_residual
 EXTRA_OPS = ("carried_up_gate_swiglu", "scaled_logits_from_carried")
 
 
-def patch_reference(engpt_pkg: ModuleType, include_extras: bool = False) -> Callable[[], None]:
+def patch_reference(engpt_pkg: ModuleType, include_extras: bool = False,
+                    via_torch_ops: bool = False) -> Callable[[], None]:
     """Rebind the reference model's op names to the engpt_b200 CUDA ops.
 
-    ``engpt_pkg`` is the imported reference package (``import engpt``).
-    Returns a function that undoes the patch.
+    ``engpt_pkg`` is the imported reference package (``import engpt``).  With
+    ``via_torch_ops`` the three hot-path names are bound to the registered
+    operators ``torch.ops.engpt_b200.*`` (same kernels, called through the
+    PyTorch dispatcher) instead of the Python functions.  Returns a function
+    that undoes the patch.
     """
     models = getattr(engpt_pkg, "models", None)
     if models is None:
         import importlib
         models = importlib.import_module(engpt_pkg.__name__ + ".models")
     names = HOT_PATH_OPS + (EXTRA_OPS if include_extras else ())
+    if via_torch_ops:
+        import torch
+        from . import torch_ops  # noqa: F401  (registers the operators)
+        impl = {n: getattr(torch.ops.engpt_b200, n) for n in HOT_PATH_OPS}
+    else:
+        impl = {}
     saved: Dict[str, object] = {}
     for name in names:
         if not hasattr(models, name):
             raise AttributeError(f"{models.__name__} has no attribute {name}; not a compatible engpt package")
         saved[name] = getattr(models, name)
-        setattr(models, name, getattr(K, name))
+        setattr(models, name, impl.get(name, getattr(K, name)))
 
     def unpatch() -> None:
         for n, fn in saved.items():

@@ -230,12 +230,30 @@ def carried_up_gate_swiglu(y: Tensor, rho: Tensor, weight: Tensor, s_u: Tensor, 
                            scale_u_by_sqrt_d: bool) -> Tensor:
     """MLP up/gate projection of ``Y/rho`` + SwiGLU -- engpt/kernels.py:182-206.
 
-    The projection is a cuBLAS GEMM (through torch, honouring autocast); the
-    scales and SiLU gate run in one CUDA epilogue kernel.
+    Under bf16 autocast (the reference's GPU flow) with a width that is a
+    multiple of 128: the tcgen05 GEMM with SwiGLU in its epilogue
+    (``engpt_up_gate_swiglu``), so the ``[.., 2W]`` projection is never
+    written; otherwise a cuBLAS GEMM (through torch, honouring autocast) and
+    the SwiGLU kernel.  The result has the reference's dtype (bf16 GEMM output
+    times fp32 scales: fp32).
     """
     _require_cuda(y, rho, weight, s_u, s_gate)
     _forward_only(y, rho, weight, s_u, s_gate)
     mlp_in = y / rho.unsqueeze(-1)
+    d = mlp_in.shape[-1]
+    width = weight.shape[0] // 2
+    if (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+            and width % 128 == 0 and d % 8 == 0 and weight.shape[1] == d):
+        x = mlp_in.reshape(-1, d).to(torch.bfloat16).contiguous()
+        w = weight.to(torch.bfloat16).contiguous()
+        hidden = torch.empty(x.shape[0], width, device=x.device, dtype=torch.bfloat16)
+        su, sg = _f32c(s_u), _f32c(s_gate)
+        with torch.cuda.device(y.device):
+            _lib.call("engpt_up_gate_swiglu", x.data_ptr(), w.data_ptr(), su.data_ptr(), sg.data_ptr(),
+                      float(sqrt_d if scale_u_by_sqrt_d else 1.0), float(sqrt_d), x.shape[0], d, width,
+                      hidden.data_ptr(), _lib.stream_handle(y.device))
+        out_dtype = torch.promote_types(torch.bfloat16, s_u.dtype)
+        return hidden.view(*mlp_in.shape[:-1], width).to(out_dtype)
     ug = torch.nn.functional.linear(mlp_in, weight).contiguous()
     width = ug.shape[-1] // 2
     out = torch.empty(*ug.shape[:-1], width, device=ug.device, dtype=torch.promote_types(ug.dtype, s_u.dtype))

@@ -456,6 +456,17 @@ class EfficientNGPT(nn.Module):
                 logits = logits.contiguous()
         return logits, loss
 
+    def last_hidden(self) -> Tensor:
+        """Represented state ``Y / rho`` after the last block of the latest forward, ``[B, T, d]``.
+
+        A view of the engine's workspace (bf16 under autocast, fp32 otherwise):
+        the operand of the output head, valid until the next forward.
+        """
+        ws = self._ws
+        if ws is None:
+            raise RuntimeError("last_hidden() needs a forward first")
+        return ws.x.view(ws.bsz, ws.seq_len, self.cfg.n_embd)
+
     def forward_with_states(self, idx: Tensor, targets: Optional[Tensor] = None):
         """Forward that also returns the per-layer carried state ``[(Y, rho), ...]`` (copies)."""
         states = []

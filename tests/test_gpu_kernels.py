@@ -617,3 +617,46 @@ def test_logits_cross_entropy_matches_unfused_path(cuda, rows, d, vocab, ld):
     _lib.call("engpt_cross_entropy", ref_logits.data_ptr(), _lib.BF16, rows, vocab, vocab, tgt.data_ptr(),
               rl2.data_ptr(), loss2.data_ptr(), _stream())
     assert abs(loss.item() - loss2.item()) < 1e-2
+
+
+def test_torch_ops_match_python_ops(cuda):
+    """torch.ops.engpt_b200.* (the registered operators) give the Python ops' results bit for bit."""
+    rng = np.random.default_rng(3)
+    B, T, H, Dh = 2, 100, 4, 64
+    qkv = t(rng.standard_normal((B, T, 3, H, Dh)), cuda, torch.bfloat16)
+    rho = t(rng.uniform(0.5, 50.0, (B, T)), cuda)
+    cos, sin = K.rotary_frequencies(T, Dh, device=cuda, dtype=torch.float32, theta=10000.0)
+    sc = t(rng.uniform(0.9, 1.1, (H, Dh)), cuda)
+    a = K.qkv_postprocess_from_carried(qkv, rho, cos, sin, sc, 1e-6)
+    b = torch.ops.engpt_b200.qkv_postprocess_from_carried(qkv, rho, cos, sin, sc, 1e-6)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    o1 = K.causal_sdpa(*a, scale=8.0, dropout_p=0.0)
+    o2 = torch.ops.engpt_b200.causal_sdpa(*b, scale=8.0, dropout_p=0.0)
+    assert torch.equal(o1, o2)
+    y = t(rng.standard_normal((B, T, 256)), cuda)
+    br = t(rng.standard_normal((B, T, 256)), cuda, torch.bfloat16)
+    al = t(rng.uniform(0, 0.1, 256), cuda)
+    r1 = K.carried_residual_gauge(y, rho, br, al, 1e-6, 1e-6, 1024.0)
+    r2 = torch.ops.engpt_b200.carried_residual_gauge(y, rho, br, al, 1e-6, 1e-6, 1024.0)
+    assert torch.equal(r1[0], r2[0]) and torch.equal(r1[1], r2[1])
+
+
+def test_carried_up_gate_swiglu_op_fused_under_autocast(cuda):
+    """The op-level MLP helper (engpt/kernels.py:182-206) under bf16 autocast runs the fused up/gate + SwiGLU
+    GEMM: result against an fp32 restatement of the reference formula on the same bf16 operands, and the
+    reference's output dtype (fp32)."""
+    g = torch.Generator().manual_seed(9)
+    B, T, d, W = 2, 96, 256, 1024
+    y = (torch.randn(B, T, d, generator=g) * 3).to(cuda)
+    rho = (torch.rand(B, T, generator=g) * 5 + 0.5).to(cuda)
+    w = (torch.randn(2 * W, d, generator=g) / 16).to(cuda)
+    su = (torch.rand(W, generator=g) + 0.5).to(cuda)
+    sg = (torch.rand(W, generator=g) + 0.5).to(cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = K.carried_up_gate_swiglu(y, rho, w, su, sg, sqrt_d=16.0, scale_u_by_sqrt_d=True)
+    assert out.dtype == torch.float32 and out.shape == (B, T, W)
+    x = (y / rho.unsqueeze(-1)).to(torch.bfloat16).float()
+    ug = x @ w.to(torch.bfloat16).float().t()
+    u, gate = ug[..., :W] * su * 16.0, ug[..., W:] * sg * 16.0
+    ref = u * torch.nn.functional.silu(gate)
+    assert ((out - ref).abs().max() / ref.abs().max()).item() < 1e-2

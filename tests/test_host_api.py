@@ -67,3 +67,52 @@ def test_patch_reference_rebinds_model_namespace():
     assert models.qkv_postprocess_from_carried is K.qkv_postprocess_from_carried
     undo()
     assert models.causal_sdpa is orig
+
+
+def test_patch_reference_via_torch_ops():
+    import torch
+    models = types.ModuleType("fake_engpt2.models")
+    for n in ("qkv_postprocess_from_carried", "causal_sdpa", "carried_residual_gauge"):
+        setattr(models, n, object())
+    pkg = types.ModuleType("fake_engpt2")
+    pkg.models = models
+    undo = patch_reference(pkg, via_torch_ops=True)
+    assert models.causal_sdpa is torch.ops.engpt_b200.causal_sdpa
+    assert models.carried_residual_gauge is torch.ops.engpt_b200.carried_residual_gauge
+    undo()
+
+
+def test_torch_ops_registered_with_reference_signatures():
+    """torch.ops.engpt_b200.* exist with the reference ops' argument lists (engpt/kernels.py:139, 277, 417)."""
+    import torch
+    import engpt_b200  # noqa: F401  (registers the operators)
+    schemas = {n: str(getattr(torch.ops.engpt_b200, n).default._schema) for n in
+               ("qkv_postprocess_from_carried", "causal_sdpa", "carried_residual_gauge")}
+    assert "(Tensor qkv, Tensor rho, Tensor cos, Tensor sin, Tensor qk_scale, float norm_eps) -> (Tensor, Tensor, Tensor)" \
+        in schemas["qkv_postprocess_from_carried"]
+    assert "(Tensor q, Tensor k, Tensor v, *, float scale, float dropout_p) -> Tensor" in schemas["causal_sdpa"]
+    assert ("(Tensor y, Tensor rho, Tensor branch, Tensor alpha, float branch_eps, float residual_eps, "
+            "float max_radius) -> (Tensor, Tensor)") in schemas["carried_residual_gauge"]
+
+
+def test_torch_ops_fake_shapes_and_no_cpu_kernel():
+    """Shape propagation without running a kernel (fake tensors), and no CPU implementation (no fallback)."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import engpt_b200  # noqa: F401
+    with FakeTensorMode():
+        qkv = torch.empty(2, 9, 3, 4, 16, device="cuda", dtype=torch.bfloat16)
+        rho = torch.empty(2, 9, device="cuda")
+        q, k, v = torch.ops.engpt_b200.qkv_postprocess_from_carried(
+            qkv, rho, torch.empty(9, 8, device="cuda"), torch.empty(9, 8, device="cuda"),
+            torch.empty(4, 16, device="cuda"), 1e-6)
+        assert q.shape == (2, 9, 4, 16) and q.dtype == torch.bfloat16
+        o = torch.ops.engpt_b200.causal_sdpa(q, k, v, scale=4.0, dropout_p=0.0)
+        assert o.shape == q.shape
+        y, r = torch.ops.engpt_b200.carried_residual_gauge(
+            torch.empty(2, 9, 64, device="cuda"), rho, torch.empty(2, 9, 64, device="cuda", dtype=torch.bfloat16),
+            torch.empty(64, device="cuda"), 1e-6, 1e-6, 1024.0)
+        assert y.shape == (2, 9, 64) and y.dtype == torch.float32 and r.shape == (2, 9)
+    x = torch.zeros(1, 4, 1, 64)
+    with pytest.raises(NotImplementedError):
+        torch.ops.engpt_b200.causal_sdpa(x, x, x, scale=8.0, dropout_p=0.0)
