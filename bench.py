@@ -56,7 +56,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-METRIC = "forward tokens/sec (EfficientNGPT bf16, L=16 d=1024 H=16 T=2048)"
+def metric_name(a):
+    return f"forward tokens/sec (EfficientNGPT bf16, L={a.layers} d={a.dim} H={a.heads} T={a.seq})"
 
 # The result line goes to the original stdout; everything else written to fd 1 (library banners such as
 # NCCL's version line, stray prints) is redirected to stderr so stdout carries exactly one JSON line.
@@ -267,7 +268,7 @@ def run_reference(a, world, rank):
     threads = _blas_threads() or cores
     sample = f"{n} x {a.seq}-token sequence(s) of the workload per step, fp32 numpy, {threads} BLAS threads"
     emit({
-        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
+        "metric": metric_name(a), "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": 1000.0 * total / a.steps, "higher_is_better": True,
         "scaling": a.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(a, world),
@@ -411,7 +412,7 @@ def run_gpu(a, world, rank, local_rank):
     achieved = attn_flops / (attn_avg / 1000.0) / 1e12
     peak = peaks["bf16_tflops_sustained"]
     out = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "metric": metric_name(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform random ids, seeded random-init unit-sphere weights)",
         "config": workload_config(a, world),

@@ -56,6 +56,11 @@ SIGNATURES = {
     "engpt_cross_entropy": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _p]),
     "engpt_logits_cross_entropy": (_i, [_p, _p, _i64, _i, _i64, _p, _i64, _p, _p, _p, _p, _p]),
     "engpt_cross_entropy_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
+    "engpt_normalize_rows": (_i, [_p, _i, _i64, _i64, _f, _p]),
+    "engpt_normalize_columns": (_i, [_p, _i, _i64, _i64, _f, _p, _p]),
+    "engpt_project_row_grad": (_i, [_p, _p, _i, _i64, _i64, _p]),
+    "engpt_project_column_grad": (_i, [_p, _p, _i, _i64, _i64, _p, _p]),
+    "engpt_column_scratch_floats": (_i64, [_i64, _i64]),
 }
 CE_NOALLOC_MAX_ROWS = 262144
 

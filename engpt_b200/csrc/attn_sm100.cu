@@ -78,6 +78,21 @@ struct Params {
 // runs the running-max softmax.
 constexpr float kStaticBoundMax = 48.0f;
 
+// Score bound of head h in log2 units (the fixed softmax offset): |q.k| <= max_i (s_qk[h,i] s_mult)^2 for q = u * s,
+// k = w * s with unit u, w (|sum u_i w_i s_i^2| <= max s^2 sum |u_i w_i| <= max s^2), times |scale| log2(e); the
+// 1/64 margin covers the bf16 rounding of q and k.  Warp-uniform (a shuffle reduction over the head's DH scales).
+template <int DH>
+__device__ __forceinline__ float head_bound(const Params& p, int h, int lane) {
+  const float* s = p.s_qk + (int64_t)h * DH;
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < DH / 32; ++i) {
+    const float a = s[lane + 32 * i] * p.s_mult;
+    m = fmaxf(m, a * a);
+  }
+  return fabsf(p.scale_log2) * warp_max(m) * (1.0f + 1.0f / 64.0f);
+}
+
 // One CTA owns a 128-query tile of one (batch, head) and walks the causal
 // prefix of 128-key tiles.  Warp roles (192 threads):
 //   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
@@ -105,6 +120,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  auto wwait = [&](uint32_t b, uint32_t parity, int site) -> bool {
+    return __all_sync(0xffffffffu, mbar_wait(b, parity, abort_flag, site));
+  };
 
   // the q tiles of one (batch, head) run back to back, heaviest (longest causal prefix) first,
   // so the K/V tiles they share are re-read from L2 rather than HBM
@@ -184,48 +202,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (whole warp, one elected lane issues)
+    {
       constexpr uint32_t kIdescS = idesc_bf16_f32(BM, BN, false, false);
       constexpr uint32_t kIdescPV = idesc_bf16_f32(BM, D, false, true);
-      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, 2);
+      bool ok = wwait(bar(B_Q), 0, 2);
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (j < n_kv) {
           const int s = j % NS;
           const int sb = j & 1;
-          ok = mbar_wait(bar(B_KFULL + s), (j / NS) & 1, abort_flag, 3);
+          ok = wwait(bar(B_KFULL + s), (j / NS) & 1, 3);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t qa = sbase + L::Q + (kk >> 2) * kBlockBytes + (kk & 3) * 32;
             const uint32_t ka = sbase + L::K + (s * L::kDB + (kk >> 2)) * kBlockBytes + (kk & 3) * 32;
-            umma_f16_ss(tS + sb * BN, sw128_desc(qa, 16, 1024), sw128_desc(ka, 16, 1024), kIdescS, kk > 0);
+            umma_f16_ss_w(tS + sb * BN, sw128_desc(qa, 16, 1024), sw128_desc(ka, 16, 1024), kIdescS, kk > 0);
           }
-          umma_commit(bar(B_SFULL + sb));
+          umma_commit_w(bar(B_SFULL + sb));
         }
         if (j >= 1) {
           const int jj = j - 1;
           const int s2 = jj % NS;
           const int pb = jj & 1;
-          ok = mbar_wait(bar(B_PFULL + pb), (jj >> 1) & 1, abort_flag, 4);
+          ok = wwait(bar(B_PFULL + pb), (jj >> 1) & 1, 4);
           if (!ok) break;
-          ok = mbar_wait(bar(B_VFULL + s2), (jj / NS) & 1, abort_flag, 5);
+          ok = wwait(bar(B_VFULL + s2), (jj / NS) & 1, 5);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             const uint32_t pa = sbase + L::P + (pb * 2 + (kk >> 2)) * kBlockBytes + (kk & 3) * 32;
             const uint32_t va = sbase + L::V + s2 * L::kDB * kBlockBytes + kk * 16 * 128;
-            umma_f16_ss(tO, sw128_desc(pa, 16, 1024), sw128_desc(va, kBlockBytes, 1024), kIdescPV,
+            umma_f16_ss_w(tO, sw128_desc(pa, 16, 1024), sw128_desc(va, kBlockBytes, 1024), kIdescPV,
                         (jj > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(bar(B_PVDONE + pb));
-          umma_commit(bar(B_KVEMPTY + s2));
+          umma_commit_w(bar(B_PVDONE + pb));
+          umma_commit_w(bar(B_KVEMPTY + s2));
         }
       }
       // all MMAs of this thread complete before TMEM is released
-      umma_commit(bar(B_FINAL));
+      umma_commit_w(bar(B_FINAL));
       volatile int never = 0;
       mbar_wait(bar(B_FINAL), 0, &never, 6);
     }
@@ -236,7 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q_idx = q0 + row;
     const uint32_t t_lane = (uint32_t)(wq * 32) << 16;
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY;
+    // with the nGPT score bound the exponent offset is fixed (no running max, no O rescale)
+    const float bound = p.s_qk ? head_bound<D>(p, h, lane) : INFINITY;
+    const bool fixed = bound <= kStaticBoundMax;
+    float m_used = fixed ? bound : -INFINITY;
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -255,10 +276,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kbase + c > q_idx) r[c] = __float_as_uint(-INFINITY);
       }
       float mx = __uint_as_float(r[0]);
+      if (!fixed) {
 #pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+      }
       const float m_new = mx * sl2;
-      if (j == 0) {
+      if (fixed) {
+      } else if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
         // raise the reference max: rescale O (complete through PV_{j-1}) and l
@@ -291,15 +315,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c8 = 0; c8 < BN / 8; ++c8) {
         float e[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = ex2_approx(fmaf(__uint_as_float(r[c8 * 8 + i]), sl2, -m_used));
-          sum += e[i];
-        }
+        for (int i = 0; i < 8; ++i) e[i] = ex2_approx(fmaf(__uint_as_float(r[c8 * 8 + i]), sl2, -m_used));
         uint4 packed;
         packed.x = pack_bf16x2(e[0], e[1]);
         packed.y = pack_bf16x2(e[2], e[3]);
         packed.z = pack_bf16x2(e[4], e[5]);
         packed.w = pack_bf16x2(e[6], e[7]);
+        // the row sum adds the bf16-rounded P that the PV product multiplies
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w2 = (&packed.x)[i];
+          sum += __uint_as_float(w2 << 16) + __uint_as_float(w2 & 0xffff0000u);
+        }
         const int blk = c8 >> 3;
         const int ch = c8 & 7;
         *reinterpret_cast<uint4*>(pbuf + blk * kBlockBytes + ((ch ^ (row & 7)) << 4)) = packed;
@@ -607,15 +633,7 @@ __device__ __forceinline__ void static_job(uint32_t tS, uint32_t tP0, int kbase,
   }
 }
 
-// Score bound of head h in log2 units: |q.k| <= max_i (s_qk[h,i] s_mult)^2 for q = u * s, k = w * s with unit
-// u, w (|sum u_i w_i s_i^2| <= max s^2 sum |u_i w_i| <= max s^2), times |scale| log2(e); the 1/64 margin covers
-// the bf16 rounding of q and k.  Warp-uniform.
-__device__ __forceinline__ float head_bound_log2(const Params& p, int h, int lane) {
-  const float* s = p.s_qk + (int64_t)h * D;
-  const float a = s[lane] * p.s_mult, b = s[lane + 32] * p.s_mult;
-  const float m = warp_max(fmaxf(a * a, b * b));
-  return fabsf(p.scale_log2) * m * (1.0f + 1.0f / 64.0f);
-}
+__device__ __forceinline__ float head_bound_log2(const Params& p, int h, int lane) { return head_bound<D>(p, h, lane); }
 
 // Band k of this CTA.  The grid is persistent (one CTA per SM) and takes the bands in rounds of gridDim.x:
 // round k covers the global band indices [k G, k G + G), in snake order (CTA c takes k G + c in even rounds,
@@ -1124,7 +1142,7 @@ static int launch_v2(const void* q, const void* k, const void* v, void* o, int B
 
 template <int D>
 static int launch(const void* q, const void* k, const void* v, void* o, int B, int T, int H, float scale,
-                  const int64_t* s, cudaStream_t st) {
+                  const int64_t* s, const float* s_qk, float s_mult, cudaStream_t st) {
   using Lt = Layout<D>;
   CUtensorMap mq, mk, mv;
   int rc;
@@ -1141,8 +1159,8 @@ static int launch(const void* q, const void* k, const void* v, void* o, int B, i
   p.H = H;
   p.n_qt = (T + BM - 1) / BM;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.s_qk = nullptr;
-  p.s_mult = 1.0f;
+  p.s_qk = s_qk;
+  p.s_mult = s_mult;
   const int64_t blocks = (int64_t)p.n_qt * B * H;
   ENGPT_REQUIRE(blocks <= 0x7fffffffLL, ENGPT_ERR_SHAPE, "attention: grid too large");
   auto kern = attn_fwd_kernel<D>;
@@ -1175,10 +1193,11 @@ extern "C" int engpt_causal_attention(const void* q, const void* k, const void* 
     int rc = attn_tc::get_encode();
     if (rc) return rc;
     if (Dh == 64) {
-      if (impl == ENGPT_ATTN_TCGEN05_1TILE) return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, st);
+      if (impl == ENGPT_ATTN_TCGEN05_1TILE)
+        return attn_tc::launch<64>(q, k, v, o, B, T, H, scale, strides, nullptr, 1.0f, st);
       return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, nullptr, 1.0f, st);
     }
-    return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, st);
+    return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, nullptr, 1.0f, st);
   }
   return launch_attn_simt(q, k, v, o, dtype, B, T, H, Dh, scale, strides, st);
 }
@@ -1193,10 +1212,12 @@ extern "C" int engpt_ngpt_attention(const void* q, const void* k, const void* v,
   ENGPT_REQUIRE(dtype == ENGPT_BF16 || dtype == ENGPT_F32, ENGPT_ERR_DTYPE, "ngpt_attention: dtype %d", dtype);
   if ((int64_t)B * T == 0) return ENGPT_OK;
   ENGPT_REQUIRE(q && k && v && o && strides, ENGPT_ERR_ARG, "ngpt_attention: null pointer");
-  if (dtype == ENGPT_BF16 && Dh == 64 && attn_tc::tc_eligible(q, k, v, o, Dh, strides)) {
+  if (dtype == ENGPT_BF16 && (Dh == 64 || Dh == 128) && attn_tc::tc_eligible(q, k, v, o, Dh, strides)) {
     int rc = attn_tc::get_encode();
     if (rc) return rc;
-    return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, qk_scale, qk_mult, as_stream(stream));
+    if (Dh == 64)
+      return attn_tc::launch_v2(q, k, v, o, B, T, H, scale, strides, qk_scale, qk_mult, as_stream(stream));
+    return attn_tc::launch<128>(q, k, v, o, B, T, H, scale, strides, qk_scale, qk_mult, as_stream(stream));
   }
   // other head dims and fp32: the general kernels (their running-max softmax is exact for any scores)
   return engpt_causal_attention(q, k, v, o, dtype, B, T, H, Dh, scale, strides, ENGPT_ATTN_AUTO, stream);

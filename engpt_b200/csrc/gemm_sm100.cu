@@ -147,7 +147,57 @@ struct QkvEpi {
   const float* sin_tab;
   const float* qk_scale;     // [H, Dh]
   float qk_mult, eps;
-  int M, T, d, rope_half;
+  int M, T, d, rope_half, dh;   // dh: head_dim, 64 or 128
+  // q or k heads of head_dim 128 (two per 256-column tile): the norm over the head's 128 accumulator columns,
+  // then two 64-column halves rotated (pairs 32 half ..), scaled and stored
+  __device__ __forceinline__ void tile128(int m0, int m, int col0, int part, uint32_t tacc, float rho_m,
+                                          OutStage& out) const {
+    const int t = m < M ? m % T : 0;
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 128; ++hh) {
+      const uint32_t th = tacc + 128 * hh;
+      float ss = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32];
+        load_acc32(th + 32 * c, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss = fmaf(x[i], x[i], ss);
+      }
+      float inv_den = rsqrtf(ss);
+      if (eps > 0.f) inv_den = fminf(inv_den, __fdividef(1.0f, rho_m * eps));
+      const float f = inv_den * qk_mult;
+      const float* sc = qk_scale + (col0 + 128 * hh - part * d);   // s_qk[h, 0..127]
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float x[64];
+        load_acc32(th + 64 * half, x);
+        load_acc32(th + 64 * half + 32, x + 32);
+        const int p0 = 32 * half;                                   // first rotary pair of this half
+        const float* crow = cos_tab + (int64_t)t * rope_half;
+        const float* srow = sin_tab + (int64_t)t * rope_half;
+        uint4 o[8];
+#pragma unroll
+        for (int i = 0; i < 64; i += 8) {
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc + 64 * half + i));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + 64 * half + i + 4));
+          const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          float v[8];
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) {
+            const int pi = p0 + ((i + k) >> 1);
+            const float c = pi < rope_half ? __ldg(crow + pi) : 1.f;
+            const float sn = pi < rope_half ? __ldg(srow + pi) : 0.f;
+            const float xe = x[i + k], xo = x[i + k + 1];
+            v[k] = ((xe * c - xo * sn) * f) * scl[k];
+            v[k + 1] = ((xe * sn + xo * c) * f) * scl[k + 1];
+          }
+          o[i / 8] = pack8(v);
+        }
+        out.put(col0 + 128 * hh + 64 * half, m0, o);
+      }
+    }
+  }
   __device__ __forceinline__ void tile(int m0, int m, int tn, uint32_t tacc, OutStage& out) const {
     const int col0 = tn * BN;
     const int part = col0 / d;            // 0: q, 1: k, 2: v (a 256-column tile lies inside one)
@@ -167,6 +217,10 @@ struct QkvEpi {
         for (int j = 0; j < 8; ++j) o[j] = pack8(x + 8 * j);
         out.put(col0 + 64 * hh, m0, o);
       }
+      return;
+    }
+    if (dh == 128) {
+      tile128(m0, m, col0, part, tacc, rho_m, out);
       return;
     }
     // this token's rotary row, once for the tile's four heads (pairs >= rope_half: cos 1, sin 0)
@@ -1007,8 +1061,8 @@ extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const floa
                                     const float* sin_tab, int rope_half, const float* qk_scale, float qk_mult,
                                     float norm_eps, int B, int T, int H, int Dh, void* qkv_out, void* stream) {
   clear_error();
-  ENGPT_REQUIRE(B >= 0 && T > 0 && H > 0 && Dh == 64, ENGPT_ERR_UNSUPPORTED,
-                "qkv_projection: head_dim %d (the fused tile needs 64)", Dh);
+  ENGPT_REQUIRE(B >= 0 && T > 0 && H > 0 && (Dh == 64 || Dh == 128), ENGPT_ERR_UNSUPPORTED,
+                "qkv_projection: head_dim %d (the fused tile needs 64 or 128)", Dh);
   const int d = H * Dh;
   ENGPT_REQUIRE(d % gemm::BN == 0, ENGPT_ERR_UNSUPPORTED, "qkv_projection: d=%d not a multiple of 256", d);
   ENGPT_REQUIRE(rope_half >= 0 && 2 * rope_half <= Dh, ENGPT_ERR_SHAPE, "qkv_projection: rope_half=%d", rope_half);
@@ -1018,7 +1072,7 @@ extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const floa
   ENGPT_REQUIRE(x && w_qkv && rho && qk_scale && qkv_out && (rope_half == 0 || (cos_tab && sin_tab)), ENGPT_ERR_ARG,
                 "qkv_projection: null pointer");
   ENGPT_REQUIRE(aligned(qkv_out, 16), ENGPT_ERR_ALIGN, "qkv_projection: output not 16-byte aligned");
-  gemm::QkvEpi epi{rho, cos_tab, sin_tab, qk_scale, qk_mult, norm_eps, (int)M, T, d, rope_half};
+  gemm::QkvEpi epi{rho, cos_tab, sin_tab, qk_scale, qk_mult, norm_eps, (int)M, T, d, rope_half, Dh};
   return gemm::launch(x, d, w_qkv, d, 3 * d, (int)M, 3 * d / gemm::BN, d, 0, gemm::BN / 2, gemm::BN, qkv_out, 3 * d,
                       3 * d, epi, as_stream(stream));
 }

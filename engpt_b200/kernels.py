@@ -23,6 +23,10 @@ from torch import Tensor
 from . import _lib
 
 __all__ = [
+    "normalize_rows_",
+    "normalize_columns_",
+    "project_row_grad_",
+    "project_column_grad_",
     "qkv_postprocess_from_carried",
     "causal_sdpa",
     "ngpt_attention_scale",
@@ -274,3 +278,67 @@ def scaled_logits_from_carried(y: Tensor, rho: Tensor, output_emb: Tensor, logit
         _lib.call("engpt_scale_rows_cast", emb32.data_ptr(), scale32.data_ptr(), 1.0, output_emb.shape[0],
                   output_emb.shape[1], w.data_ptr(), _lib.dtype_code(w.dtype), _lib.stream_handle(y.device))
     return torch.nn.functional.linear(h.to(w.dtype), w)
+
+
+# ------------------------------------------------------------ optimizer-side sphere operations
+def _sphere_matrix(x: Tensor, what: str) -> None:
+    if not x.is_cuda:
+        raise RuntimeError("engpt_b200 ops run on CUDA tensors only (no CPU fallback)")
+    if x.ndim != 2 or not x.is_contiguous():
+        raise ValueError(f"{what}: needs a contiguous 2-D matrix, got shape {tuple(x.shape)}")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise NotImplementedError(f"{what}: float32 and bfloat16 only, got {x.dtype}")
+
+
+@torch.no_grad()
+def normalize_rows_(x: Tensor, eps: float = 1e-12) -> Tensor:
+    """In place: every row to unit L2 norm, ``x[r] /= max(|x[r]|, eps)`` -- engpt/kernels.py:98-105."""
+    _sphere_matrix(x, "normalize_rows_")
+    with torch.cuda.device(x.device):
+        _lib.call("engpt_normalize_rows", x.data_ptr(), _lib.dtype_code(x.dtype), x.shape[0], x.shape[1],
+                  float(eps), _lib.stream_handle(x.device))
+    return x
+
+
+def _column_scratch(x: Tensor) -> Tensor:
+    n = int(_lib.load().engpt_column_scratch_floats(x.shape[0], x.shape[1]))
+    return torch.empty(max(n, 1), device=x.device, dtype=torch.float32)
+
+
+@torch.no_grad()
+def normalize_columns_(x: Tensor, eps: float = 1e-12) -> Tensor:
+    """In place: every column to unit L2 norm, ``x[:, c] /= max(|x[:, c]|, eps)`` -- engpt/kernels.py:108-116."""
+    _sphere_matrix(x, "normalize_columns_")
+    scratch = _column_scratch(x)
+    with torch.cuda.device(x.device):
+        _lib.call("engpt_normalize_columns", x.data_ptr(), _lib.dtype_code(x.dtype), x.shape[0], x.shape[1],
+                  float(eps), scratch.data_ptr(), _lib.stream_handle(x.device))
+    return x
+
+
+def _check_pair(weight: Tensor, grad: Tensor, what: str) -> None:
+    _sphere_matrix(weight, what)
+    _sphere_matrix(grad, what)
+    if weight.shape != grad.shape or weight.dtype != grad.dtype or weight.device != grad.device:
+        raise ValueError(f"{what}: weight and grad must share shape, dtype and device")
+
+
+@torch.no_grad()
+def project_row_grad_(weight: Tensor, grad: Tensor) -> None:
+    """In place: ``grad[r] -= (grad[r] . weight[r]) weight[r]`` (tangent space of unit rows) --
+    engpt/kernels.py:119-125."""
+    _check_pair(weight, grad, "project_row_grad_")
+    with torch.cuda.device(grad.device):
+        _lib.call("engpt_project_row_grad", weight.data_ptr(), grad.data_ptr(), _lib.dtype_code(grad.dtype),
+                  grad.shape[0], grad.shape[1], _lib.stream_handle(grad.device))
+
+
+@torch.no_grad()
+def project_column_grad_(weight: Tensor, grad: Tensor) -> None:
+    """In place: ``grad[:, c] -= (grad[:, c] . weight[:, c]) weight[:, c]`` (tangent space of unit columns) --
+    engpt/kernels.py:128-136."""
+    _check_pair(weight, grad, "project_column_grad_")
+    scratch = _column_scratch(grad)
+    with torch.cuda.device(grad.device):
+        _lib.call("engpt_project_column_grad", weight.data_ptr(), grad.data_ptr(), _lib.dtype_code(grad.dtype),
+                  grad.shape[0], grad.shape[1], scratch.data_ptr(), _lib.stream_handle(grad.device))

@@ -47,14 +47,21 @@ def _ngpt_base_scale(cfg: ModelConfig) -> float:
 
 @torch.no_grad()
 def _normalize_rows_(x: Tensor, eps: float) -> None:
-    # parameter retraction used at init (engpt/kernels.py:98-105, PyTorch path)
-    x.div_(torch.linalg.vector_norm(x, ord=2, dim=-1, keepdim=True).clamp_min(eps))
+    # parameter retraction (engpt/kernels.py:98-105): the CUDA kernel for CUDA parameters; on the CPU (the
+    # seeded init, which must reproduce the reference's weights bit for bit) the reference's PyTorch expression
+    if x.is_cuda:
+        K.normalize_rows_(x, eps)
+    else:
+        x.div_(torch.linalg.vector_norm(x, ord=2, dim=-1, keepdim=True).clamp_min(eps))
 
 
 @torch.no_grad()
 def _normalize_columns_(x: Tensor, eps: float) -> None:
-    # engpt/kernels.py:108-116, PyTorch path
-    x.div_(torch.linalg.vector_norm(x, ord=2, dim=0, keepdim=True).clamp_min(eps))
+    # engpt/kernels.py:108-116, as _normalize_rows_
+    if x.is_cuda:
+        K.normalize_columns_(x, eps)
+    else:
+        x.div_(torch.linalg.vector_norm(x, ord=2, dim=0, keepdim=True).clamp_min(eps))
 
 
 class EfficientNGPTBlock(nn.Module):
@@ -194,8 +201,8 @@ class EfficientNGPT(nn.Module):
         self.attn_impl = _lib.ATTN_AUTO
         # bf16 mode: up/gate projection and SwiGLU in one tcgen05 GEMM (False: cuBLAS + SwiGLU kernel)
         self.fuse_mlp = True
-        # bf16 mode, head_dim 64: QKV projection and its post-process in one tcgen05 GEMM (False: cuBLAS +
-        # the QKV epilogue kernel in place)
+        # bf16 mode, head_dim 64 or 128: QKV projection and its post-process in one tcgen05 GEMM (False:
+        # cuBLAS + the QKV epilogue kernel in place)
         self.fuse_qkv = True
         # bf16 mode, d in {256, 512, 768, 1024}: out_proj / down_proj GEMMs with the carried residual in
         # their epilogue (engpt_gemm_carried_residual).  Off by default: at d=1024, T=2048, B=32 it measures
@@ -356,7 +363,7 @@ class EfficientNGPT(nn.Module):
                 else:
                     wq, wo, wug, wd = blk.qkv.weight, blk.out_proj.weight, blk.up_gate.weight, blk.down_proj.weight
                     x_in = ws.y
-                if bf16 and self.fuse_qkv and Dh == 64 and d % 256 == 0:
+                if bf16 and self.fuse_qkv and Dh in (64, 128) and d % 256 == 0:
                     # QKV GEMM with the post-process fused into its epilogue (tcgen05): q|k|v rows are
                     # written post-processed into the same [n, 3, H, Dh] buffer
                     _lib.call("engpt_qkv_projection", x_in.data_ptr(), wq.data_ptr(), ws.rho.data_ptr(),

@@ -135,12 +135,12 @@ ENGPT_API int engpt_causal_attention(const void* q, const void* k, const void* v
  * q and k of head h must be unit vectors (per head) multiplied elementwise
  * by qk_scale[h, :] * qk_mult (qk_scale [H, Dh] fp32 on the device), which is
  * what the QKV post-process produces.  Then every score satisfies
- * |q.k| <= max_i (qk_scale[h, i] qk_mult)^2, and the head_dim-64 bf16 kernel
- * exponentiates against that fixed per-head bound instead of a running row
- * maximum (no rescaling of P, l or O).  The bound is read on the device (no
- * host synchronisation).  A head whose bound exceeds 48 in log2 units
- * (scale * log2(e) * max s^2) runs the running-max softmax, as do other head
- * dims and fp32 (the engpt_causal_attention kernels).
+ * |q.k| <= max_i (qk_scale[h, i] qk_mult)^2, and the bf16 kernels for head_dim
+ * 64 and 128 exponentiate against that fixed per-head bound instead of a
+ * running row maximum (no rescaling of P, l or O).  The bound is read on the
+ * device (no host synchronisation).  A head whose bound exceeds 48 in log2
+ * units (scale * log2(e) * max s^2) runs the running-max softmax, as do other
+ * head dims and fp32 (the engpt_causal_attention kernels).
  */
 ENGPT_API int engpt_ngpt_attention(const void* q, const void* k, const void* v, void* o, int dtype, int B, int T,
                                    int H, int Dh, float scale, const int64_t* strides, const float* qk_scale,
@@ -217,7 +217,7 @@ ENGPT_API int engpt_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t
  * (engpt/kernels.py:139-179) on the fp32 accumulator: x [B*T, d] bf16,
  * w_qkv [3d, d] bf16; writes the post-processed q | k | v rows into qkv_out
  * [B*T, 3, H, Dh] bf16 (the layout engpt_qkv_postprocess leaves in place).
- * head_dim 64, d a multiple of 256.
+ * head_dim 64 or 128, d a multiple of 256.
  */
 ENGPT_API int engpt_qkv_projection(const void* x, const void* w_qkv, const float* rho, const float* cos_tab,
                                    const float* sin_tab, int rope_half, const float* qk_scale, float qk_mult,
@@ -266,6 +266,34 @@ ENGPT_API int engpt_gemm_carried_residual(const void* a, int64_t lda, const void
 ENGPT_API int engpt_logits_cross_entropy(const void* x, const void* w_head, int64_t rows, int d, int64_t vocab,
                                          void* logits, int64_t ld, const int64_t* targets, void* partials,
                                          float* row_loss, float* loss_out, void* stream);
+
+/*
+ * Optimizer-side sphere operations of nGPT training (NGPTAdamW,
+ * engpt/optim.py:74-109), in place on a [rows, cols] row-major matrix of
+ * `dtype` (ENGPT_F32 or ENGPT_BF16), computed in fp32:
+ *
+ * normalize_rows_ -- engpt/kernels.py:98-105 (Triton _row_normalize_kernel
+ *   32-42): x[r, :] /= max(|x[r, :]|, eps).
+ * normalize_columns_ -- engpt/kernels.py:108-116 (_column_normalize_kernel
+ *   44-55): x[:, c] /= max(|x[:, c]|, eps).
+ * project_row_grad_ -- engpt/kernels.py:119-125 (_row_grad_project_kernel
+ *   57-67): grad[r, :] -= (grad[r, :] . weight[r, :]) weight[r, :].
+ * project_column_grad_ -- engpt/kernels.py:128-136
+ *   (_column_grad_project_kernel 69-81): grad[:, c] -= (grad[:, c] .
+ *   weight[:, c]) weight[:, c].
+ *
+ * weight and grad share the dtype and shape.  The column forms read each
+ * column tile in row splits and take caller scratch of
+ * engpt_column_scratch_floats(rows, cols) floats for the partial sums.
+ */
+ENGPT_API int engpt_normalize_rows(void* x, int dtype, int64_t rows, int64_t cols, float eps, void* stream);
+ENGPT_API int engpt_normalize_columns(void* x, int dtype, int64_t rows, int64_t cols, float eps, float* scratch,
+                                      void* stream);
+ENGPT_API int engpt_project_row_grad(const void* weight, void* grad, int dtype, int64_t rows, int64_t cols,
+                                     void* stream);
+ENGPT_API int engpt_project_column_grad(const void* weight, void* grad, int dtype, int64_t rows, int64_t cols,
+                                        float* scratch, void* stream);
+ENGPT_API int64_t engpt_column_scratch_floats(int64_t rows, int64_t cols);
 
 /*
  * Token cross-entropy -- engpt/models.py:328-333 (F.cross_entropy, mean).

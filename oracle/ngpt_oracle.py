@@ -170,6 +170,27 @@ def reference_residual(h: Array, branch: Array, alpha: Array, branch_eps: float,
     return normalize_last_dim(mixed, residual_eps)
 
 
+def normalize_rows(x: Array, eps: float) -> Array:
+    """Rows to unit L2 norm: ``x / max(|x_row|, eps)``; engpt/kernels.py:98-105 (and its Triton kernel 32-42,
+    whose ``sqrt(max(ss, eps^2))`` is the same denominator)."""
+    return x / np.maximum(np.sqrt(np.sum(x * x, axis=-1, keepdims=True)), eps)
+
+
+def normalize_columns(x: Array, eps: float) -> Array:
+    """Columns to unit L2 norm; engpt/kernels.py:108-116 (Triton kernel 44-55)."""
+    return x / np.maximum(np.sqrt(np.sum(x * x, axis=0, keepdims=True)), eps)
+
+
+def project_row_grad(weight: Array, grad: Array) -> Array:
+    """``grad - (grad . w)_row w``: the tangent space of unit rows; engpt/kernels.py:119-125 (Triton 57-67)."""
+    return grad - np.sum(grad * weight, axis=-1, keepdims=True) * weight
+
+
+def project_column_grad(weight: Array, grad: Array) -> Array:
+    """``grad - w (grad . w)_column``: the tangent space of unit columns; engpt/kernels.py:128-136 (Triton 69-81)."""
+    return grad - weight * np.sum(grad * weight, axis=0, keepdims=True)
+
+
 def silu(x: Array) -> Array:
     return x / (1.0 + np.exp(-x))
 

@@ -4,7 +4,7 @@ Usage (needs the Pi-Willie/enGPT sources, not needed at test time)::
 
     PYTHONPATH=<enGPT checkout> python tests/golden/make_golden.py [name ...]
 
-With names (ops, small, attn, cfg1, cfg4, cfg3, cfg5) only those fixtures are
+With names (ops, small, attn, sphere, optim, cfg1, cfg4, cfg3, cfg5) only those fixtures are
 written; with none, all of them.
 
 The reference is run on the CPU (fp64 for the op-level and small-model
@@ -88,6 +88,47 @@ def ops_vectors(K):
         out.update({f"sdpa_{tag}_q": q.numpy(), f"sdpa_{tag}_k": k.numpy(),
                     f"sdpa_{tag}_v": v.numpy(), f"sdpa_{tag}_o": o.numpy()})
     np.savez_compressed(os.path.join(HERE, "ops_small.npz"), **out)
+
+
+def sphere_vectors(K):
+    """Retraction and tangent projection (engpt/kernels.py:98-136) on odd and ragged shapes, fp64, and one
+    NGPTAdamW step (engpt/optim.py:38-67) of the reference's small model with seeded gradients."""
+    out = {}
+    g = torch.Generator().manual_seed(13)
+    for tag, shape in {"a": (9, 13), "b": (33, 100), "c": (130, 7)}.items():
+        w = torch.randn(*shape, generator=g, dtype=torch.float64)
+        gr = torch.randn(*shape, generator=g, dtype=torch.float64)
+        out[f"sph_{tag}_w"] = w.numpy()
+        out[f"sph_{tag}_g"] = gr.numpy()
+        out[f"sph_{tag}_rows"] = K.normalize_rows_(w.clone(), 1e-6).numpy()
+        out[f"sph_{tag}_cols"] = K.normalize_columns_(w.clone(), 1e-6).numpy()
+        wr = K.normalize_rows_(w.clone(), 1e-12)
+        wc = K.normalize_columns_(w.clone(), 1e-12)
+        pr, pc = gr.clone(), gr.clone()
+        K.project_row_grad_(wr, pr)
+        K.project_column_grad_(wc, pc)
+        out[f"sph_{tag}_wr"] = wr.numpy()
+        out[f"sph_{tag}_wc"] = wc.numpy()
+        out[f"sph_{tag}_prow"] = pr.numpy()
+        out[f"sph_{tag}_pcol"] = pc.numpy()
+    np.savez_compressed(os.path.join(HERE, "sphere_small.npz"), **out)
+
+
+def optimizer_step(EfficientNGPT, ModelConfig):
+    """One NGPTAdamW step (engpt/optim.py:38-67) of the reference's small config in fp32 with seeded gradients."""
+    from engpt.optim import NGPTAdamW
+    cfg = ModelConfig(vocab_size=64, block_size=16, n_layer=2, n_head=2, n_embd=32, mlp_ratio=2.0, dropout=0.0)
+    torch.manual_seed(2)
+    model = EfficientNGPT(cfg)
+    g = torch.Generator().manual_seed(14)
+    grads = {n: torch.randn(p.shape, generator=g) * 0.1 for n, p in model.named_parameters()}
+    for n, p in model.named_parameters():
+        p.grad = grads[n].clone()
+    opt = NGPTAdamW(model, lr=1e-2)
+    opt.step()
+    out = {"g:" + n: v.numpy() for n, v in grads.items()}
+    out.update({"w:" + n: p.detach().numpy() for n, p in model.named_parameters()})
+    np.savez_compressed(os.path.join(HERE, "optim_step.npz"), **out)
 
 
 def capture_states(model, fn):
@@ -189,6 +230,8 @@ def main():
         "ops": lambda: ops_vectors(K),
         "small": lambda: model_small(EfficientNGPT, ModelConfig),
         "attn": lambda: isolated_attention(K),
+        "sphere": lambda: sphere_vectors(K),
+        "optim": lambda: optimizer_step(EfficientNGPT, ModelConfig),
         "cfg1": lambda: model_config(EfficientNGPT, ModelConfig, "cfg1", V=50257, L=4, H=4, d=256, T=256, B=16,
                                      state_layers=[0, 1, 2, 3], row_stride=16),
         "cfg4": lambda: model_config(EfficientNGPT, ModelConfig, "cfg4_deep", V=50257, L=128, H=4, d=256, T=256,

@@ -224,20 +224,22 @@ def _ngpt_attention(cuda, qb, kb, vb, s_raw, mult, scale):
     return o
 
 
-@pytest.mark.parametrize("B,T,H", [(2, 1, 3), (2, 100, 3), (2, 128, 3), (1, 130, 2), (2, 333, 3), (2, 1024, 4),
-                                   (8, 1200, 16), (4, 2048, 16)])
-def test_ngpt_attention_fixed_offset_vs_oracle(cuda, B, T, H):
-    """Head_dim-64 kernel with the softmax offset taken from the per-head score bound (no running max), against
-    the fp64 oracle on the same bf16 inputs: within torch's own bf16 SDPA error, as the general kernel."""
-    D = 64
+@pytest.mark.parametrize("B,T,H,D", [(2, 1, 3, 64), (2, 100, 3, 64), (2, 128, 3, 64), (1, 130, 2, 64), (2, 333, 3, 64),
+                                     (2, 1024, 4, 64), (8, 1200, 16, 64), (4, 2048, 16, 64), (2, 1, 2, 128),
+                                     (2, 333, 3, 128), (1, 2048, 4, 128)])
+def test_ngpt_attention_fixed_offset_vs_oracle(cuda, B, T, H, D):
+    """The tcgen05 kernels (head_dim 64 and 128) with the softmax offset taken from the per-head score bound (no
+    running max), against the fp64 oracle on the same bf16 inputs: within torch's own bf16 SDPA error, as the
+    general kernels."""
     q, k, v, s = _ngpt_inputs(B, T, H, D, [1.0] * H, seed=B * T + H)
     qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
-    o = _ngpt_attention(cuda, qb, kb, vb, s / 32.0, 32.0, 8.0)       # raw parameter x multiplier
-    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), 8.0)
+    scale = math.sqrt(D)
+    o = _ngpt_attention(cuda, qb, kb, vb, s / 32.0, 32.0, scale)       # raw parameter x multiplier
+    ref = O.causal_attention(*(x.float().cpu().numpy().astype(np.float64) for x in (qb, kb, vb)), scale)
     err = np.abs(o.float().cpu().numpy() - ref).max()
     sd = torch.nn.functional.scaled_dot_product_attention(qb.transpose(1, 2), kb.transpose(1, 2),
                                                           vb.transpose(1, 2), is_causal=True,
-                                                          scale=8.0).transpose(1, 2)
+                                                          scale=scale).transpose(1, 2)
     err_torch = np.abs(sd.float().cpu().numpy() - ref).max()
     assert err < 1.5e-2, (err, err_torch)
     assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
@@ -473,12 +475,11 @@ def test_qkv_projection_matches_unfused_path(cuda, B, T):
     assert diff <= 2e-2 * unf.float().abs().max().item(), diff
 
 
-@pytest.mark.parametrize("B,T", [(2, 2048), (1, 300)])
-def test_qkv_projection_vs_oracle_d1024(cuda, B, T):
-    """Fused QKV GEMM + post-process at the benchmarked width (d=1024, H=16, Dh=64) against the fp64 oracle
-    (engpt/kernels.py:139-179 on the exact product of the bf16 operands): every q/k/v row within bf16 output
-    rounding, 8e-3 of its norm."""
-    H, Dh = 16, 64
+@pytest.mark.parametrize("B,T,H,Dh", [(2, 2048, 16, 64), (1, 300, 16, 64), (1, 1024, 8, 128), (2, 130, 4, 128)])
+def test_qkv_projection_vs_oracle_d1024(cuda, B, T, H, Dh):
+    """Fused QKV GEMM + post-process against the fp64 oracle (engpt/kernels.py:139-179 on the exact product of
+    the bf16 operands) at the benchmarked width (d=1024, H=16, Dh=64) and with head_dim 128 (the long-context
+    configuration's heads): every q/k/v row within bf16 output rounding, 8e-3 of its norm."""
     d = H * Dh
     n = B * T
     g = torch.Generator().manual_seed(B * T)

@@ -151,3 +151,32 @@ def test_cfg4_deep_fp32_forward_matches_reference(golden):
         assert row_rel_err(y[0, rows] / r[0, rows][:, None], g[f"h{i}"]) < 1e-4
         assert float(r.max()) <= 1024.0 * (1 + 1e-6)
     assert float(g["rhomax8"]) == pytest.approx(1024.0)
+
+
+def test_oracle_sphere_ops_match_reference(golden):
+    """Retraction and tangent projection (engpt/kernels.py:98-136) of the oracle vs the reference's outputs."""
+    g = golden("sphere_small.npz")
+    for tag in ("a", "b", "c"):
+        w, gr = g[f"sph_{tag}_w"], g[f"sph_{tag}_g"]
+        np.testing.assert_allclose(O.normalize_rows(w, 1e-6), g[f"sph_{tag}_rows"], rtol=1e-13, atol=1e-15)
+        np.testing.assert_allclose(O.normalize_columns(w, 1e-6), g[f"sph_{tag}_cols"], rtol=1e-13, atol=1e-15)
+        np.testing.assert_allclose(O.project_row_grad(g[f"sph_{tag}_wr"], gr), g[f"sph_{tag}_prow"], rtol=1e-12,
+                                   atol=1e-13)
+        np.testing.assert_allclose(O.project_column_grad(g[f"sph_{tag}_wc"], gr), g[f"sph_{tag}_pcol"], rtol=1e-12,
+                                   atol=1e-13)
+
+
+def test_optimizer_step_host_logic_matches_reference_on_cpu(golden):
+    """engpt_b200.optim.NGPTAdamW on CPU parameters (its PyTorch expressions, the reference's CPU path) reproduces
+    the reference's NGPTAdamW step (engpt/optim.py:38-67) from the same seeded weights and gradients."""
+    from engpt_b200 import EfficientNGPT, ModelConfig
+    from engpt_b200.optim import NGPTAdamW
+    g = golden("optim_step.npz")
+    cfg = ModelConfig(vocab_size=64, block_size=16, n_layer=2, n_head=2, n_embd=32, mlp_ratio=2.0, dropout=0.0)
+    torch.manual_seed(2)
+    model = EfficientNGPT(cfg)
+    for n, p in model.named_parameters():
+        p.grad = torch.as_tensor(g["g:" + n]).clone()
+    NGPTAdamW(model, lr=1e-2).step()
+    for n, p in model.named_parameters():
+        np.testing.assert_allclose(p.detach().numpy(), g["w:" + n], rtol=1e-6, atol=1e-7)
