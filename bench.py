@@ -98,6 +98,9 @@ def parse_args():
                     help="attention workload: nGPT score-bound offset (the forward's call) or running-max softmax")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: --batch sequences in total, split over the ranks; weak: --batch per rank")
+    ap.add_argument("--head-split", type=int, default=1,
+                    help="ranks per head-split group: each group of this many GPUs shares its sequences' heads and "
+                         "MLP units (two all-reduces per layer); the batch is split over the groups")
     ap.add_argument("--gather", choices=["hidden", "logits", "none"], default="hidden",
                     help="N>1: outputs all-gathered over NCCL inside the timed step (final Y/rho, or the logits)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
@@ -108,14 +111,18 @@ def parse_args():
 
 
 def workload_config(a, world):
-    gb = a.batch if a.scaling == "strong" else a.batch * world
+    hs = getattr(a, "head_split", 1)
+    gb = a.batch if a.scaling == "strong" else a.batch * (world // hs)
     return {
         "workload": (f"EfficientNGPT forward + cross-entropy, bf16 autocast, L={a.layers} d={a.dim} H={a.heads} "
                      f"T={a.seq} V={a.vocab}, {gb} sequences in total"),
         "global_batch": gb,
         "seq_len": a.seq,
-        "parallelism": (f"dp{world}: the batch split by sequences over the ranks ({a.scaling} scaling), no "
-                        f"collective inside the forward"
+        "parallelism": ((f"dp{world // hs} x head split {hs}: groups of {hs} GPUs share each sequence's heads and MLP "
+                         f"units (two all-reduces of the partial branch per layer), the batch split over the groups"
+                         if hs > 1 else
+                         f"dp{world}: the batch split by sequences over the ranks, no collective inside the forward")
+                        + f" ({a.scaling} scaling)"
                         + (f"; per step one all-reduce of the loss and an all-gather of the {a.gather} outputs"
                            if world > 1 and a.gather != "none" else "")),
         "l2": "no flush: activations per step (~10 GB at 32 sequences) exceed the 126 MB L2",
@@ -294,11 +301,20 @@ def run_gpu(a, world, rank, local_rank):
     cfg = model_config(a)
     torch.manual_seed(0)
     model = EfficientNGPT(cfg).to(dev).eval().requires_grad_(False)
-    # the global batch: `batch` sequences split over the ranks (strong scaling), or `batch` per rank (weak)
-    global_batch = a.batch if a.scaling == "strong" else a.batch * world
+    # head-split groups of `hs` ranks share sequences; the batch is split over the world // hs groups
+    hs = a.head_split
+    replicas, replica = world // hs, rank // hs
+    dp_group = None
+    if hs > 1:
+        from engpt_b200.head_split import HeadSplit, pair_groups
+        split_groups, dp_groups = pair_groups(world, hs)
+        model.set_head_split(HeadSplit(rank % hs, hs, split_groups[replica]))
+        dp_group = dp_groups[rank % hs]
+    # the global batch: `batch` sequences split over the replicas (strong scaling), or `batch` per replica (weak)
+    global_batch = a.batch if a.scaling == "strong" else a.batch * replicas
     gen = torch.Generator().manual_seed(1000)
     idx_all = torch.randint(0, cfg.vocab_size, (global_batch, a.seq), generator=gen)
-    lo, hi = sharding.shard_range(global_batch, rank, world)
+    lo, hi = sharding.shard_range(global_batch, replica, replicas)
     if hi - lo == 0:
         raise SystemExit(f"rank {rank}: no sequences (global batch {global_batch} < {world} ranks)")
     idx_h = idx_all[lo:hi].contiguous()
@@ -316,7 +332,8 @@ def run_gpu(a, world, rank, local_rank):
 
     _lib.call = counting_call
 
-    n_valid = sharding.valid_targets(tgt_d)  # this shard's counted targets (device scalar)
+    # this shard's counted targets (device scalar); a head-split group counts its sequences once
+    n_valid = sharding.valid_targets(tgt_d) * (1 if rank % hs == 0 else 0)
 
     def step(idx, tgt):
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
@@ -327,9 +344,9 @@ def run_gpu(a, world, rank, local_rank):
             # shard gathered over NCCL: the final represented state [B, T, d] bf16, or the logits
             loss = sharding.combine_loss(loss, n_valid)
             if a.gather == "hidden":
-                out = sharding.gather_rows(model.last_hidden(), global_batch)
+                out = sharding.gather_rows(model.last_hidden(), global_batch, group=dp_group)
             elif a.gather == "logits":
-                out = sharding.gather_rows(logits, global_batch)
+                out = sharding.gather_rows(logits, global_batch, group=dp_group)
         return out, loss
 
     for _ in range(max(a.warmup, 1)):
@@ -387,7 +404,7 @@ def run_gpu(a, world, rank, local_rank):
     e2e_ms = e0.elapsed_time(e1)
 
     # per-kernel averages of the CUDA kernels (one instrumented forward, outside the timed region)
-    kern = profile_kernels(model, step, idx_d, tgt_d, cfg, a, local_batch)
+    kern = profile_kernels(model, step, idx_d, tgt_d, cfg, a, local_batch, hs)
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, attn_avg], device=dev)
@@ -408,7 +425,8 @@ def run_gpu(a, world, rank, local_rank):
     e2e = tokens / (e2e_ms / 1000.0)
     peaks = load_peaks()
     Dh = a.dim // a.heads
-    attn_flops = 2.0 * local_batch * a.heads * a.seq * a.seq * Dh  # causal: QK^T and PV over the lower triangle
+    # causal: QK^T and PV over the lower triangle, this rank's heads
+    attn_flops = 2.0 * local_batch * (a.heads // hs) * a.seq * a.seq * Dh
     achieved = attn_flops / (attn_avg / 1000.0) / 1e12
     peak = peaks["bf16_tflops_sustained"]
     out = {
@@ -416,7 +434,8 @@ def run_gpu(a, world, rank, local_rank):
         "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform random ids, seeded random-init unit-sphere weights)",
         "config": workload_config(a, world),
-        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * global_batch * a.seq * idx_h.element_size(),
+        "e2e": {"value": e2e, "unit": UNIT,
+                "h2d_bytes_per_step": 2 * global_batch * hs * a.seq * idx_h.element_size(),
                 "d2h_bytes_per_step": 4 * world},
         "gpu_launches": launches,
         "roofline": {"kernel": "attn_fwd2_kernel (tcgen05, head_dim 64)", "bound": "tensor", "achieved": achieved,
@@ -519,7 +538,7 @@ def reference_gpu_timing(a, dev, model):
     return out
 
 
-def profile_kernels(model, step, idx, tgt, cfg, a, local_batch):
+def profile_kernels(model, step, idx, tgt, cfg, a, local_batch, hs=1):
     """Average device time per launch of each C-ABI entry point over one forward (events around each call)."""
     import torch
     from engpt_b200 import _lib
@@ -548,16 +567,17 @@ def profile_kernels(model, step, idx, tgt, cfg, a, local_batch):
     # algorithmic bytes per launch (dtypes as used by the engine)
     alg = {
         "engpt_carried_residual_gauge": (4 + 2 + 4 + 2) * n * d + 8 * n,   # Y in/out fp32, branch + aux bf16
-        "engpt_qkv_postprocess": 12 * n * d + 4 * n,                      # qkv bf16 in, q/k/v bf16 out, rho
-        "engpt_swiglu": (4 + 2) * n * 4 * d,                              # ug bf16 in (2W), out bf16 (W)
+        "engpt_qkv_postprocess": 12 * n * d // hs + 4 * n,                # qkv bf16 in, q/k/v bf16 out, rho
+        "engpt_swiglu": (4 + 2) * n * 4 * d // hs,                        # ug bf16 in (2W), out bf16 (W)
         "engpt_cross_entropy": 2 * n * a.vocab + 12 * n,
         "engpt_embed_carried": (4 + 4 + 2) * n * d + 12 * n,
-        "engpt_cast_f32_bf16_many": 6 * 16 * a.layers * d * d,            # fp32 weights in, bf16 out
+        # fp32 weights in, bf16 out (a head-split rank casts its QKV and up/gate rows, all of out_proj / down)
+        "engpt_cast_f32_bf16_many": 6 * a.layers * d * d * ((3 + 8) / hs + 5),
     }
     W = 4 * d
     flops = {   # tensor-bound fused GEMMs: 2 * M * N * K
-        "engpt_qkv_projection": 2.0 * n * 3 * d * d,
-        "engpt_up_gate_swiglu": 2.0 * n * 2 * W * d,
+        "engpt_qkv_projection": 2.0 * n * 3 * d * d / hs,
+        "engpt_up_gate_swiglu": 2.0 * n * 2 * W * d / hs,
         "engpt_logits_cross_entropy": 2.0 * n * a.vocab * d,         # output head (+ log-sum-exp epilogue)
     }
     out = {}

@@ -49,7 +49,7 @@ SIGNATURES = {
     "engpt_scale_rows_cast": (_i, [_p, _p, _f, _i64, _i64, _p, _i, _p]),
     "engpt_cast_f32_bf16_many": (_i, [_p, _p, _p, _i, _p]),
     "engpt_gemm_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _i, _i, _i, _p]),
-    "engpt_qkv_projection": (_i, [_p, _p, _p, _p, _p, _i, _p, _f, _f, _i, _i, _i, _i, _p, _p]),
+    "engpt_qkv_projection": (_i, [_p, _i, _p, _p, _p, _p, _i, _p, _f, _f, _i, _i, _i, _i, _p, _p]),
     "engpt_up_gate_swiglu": (_i, [_p, _p, _p, _p, _f, _f, _i64, _i, _i, _p, _p]),
     "engpt_gemm_carried_residual": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _p, _f, _i, _f, _f, _f, _i64, _i, _p, _p,
                                          _p, _i, _p]),

@@ -390,7 +390,7 @@ extern "C" {
 
 const char* engpt_last_error(void) { return t_err; }
 
-int engpt_abi_version(void) { return 100; }
+int engpt_abi_version(void) { return 101; }
 
 int engpt_device_status(void) {
   cudaError_t e = cudaDeviceSynchronize();

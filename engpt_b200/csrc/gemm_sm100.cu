@@ -1057,14 +1057,17 @@ extern "C" int engpt_gemm_bf16(const void* a, int64_t lda, const void* b, int64_
                       epi, as_stream(stream));
 }
 
-extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const float* rho, const float* cos_tab,
-                                    const float* sin_tab, int rope_half, const float* qk_scale, float qk_mult,
-                                    float norm_eps, int B, int T, int H, int Dh, void* qkv_out, void* stream) {
+extern "C" int engpt_qkv_projection(const void* x, int in_features, const void* w_qkv, const float* rho,
+                                    const float* cos_tab, const float* sin_tab, int rope_half, const float* qk_scale,
+                                    float qk_mult, float norm_eps, int B, int T, int H, int Dh, void* qkv_out,
+                                    void* stream) {
   clear_error();
   ENGPT_REQUIRE(B >= 0 && T > 0 && H > 0 && (Dh == 64 || Dh == 128), ENGPT_ERR_UNSUPPORTED,
                 "qkv_projection: head_dim %d (the fused tile needs 64 or 128)", Dh);
   const int d = H * Dh;
   ENGPT_REQUIRE(d % gemm::BN == 0, ENGPT_ERR_UNSUPPORTED, "qkv_projection: d=%d not a multiple of 256", d);
+  ENGPT_REQUIRE(in_features > 0 && in_features % 8 == 0, ENGPT_ERR_SHAPE, "qkv_projection: in_features=%d",
+                in_features);
   ENGPT_REQUIRE(rope_half >= 0 && 2 * rope_half <= Dh, ENGPT_ERR_SHAPE, "qkv_projection: rope_half=%d", rope_half);
   const int64_t M = (int64_t)B * T;
   if (M == 0) return ENGPT_OK;
@@ -1073,8 +1076,8 @@ extern "C" int engpt_qkv_projection(const void* x, const void* w_qkv, const floa
                 "qkv_projection: null pointer");
   ENGPT_REQUIRE(aligned(qkv_out, 16), ENGPT_ERR_ALIGN, "qkv_projection: output not 16-byte aligned");
   gemm::QkvEpi epi{rho, cos_tab, sin_tab, qk_scale, qk_mult, norm_eps, (int)M, T, d, rope_half, Dh};
-  return gemm::launch(x, d, w_qkv, d, 3 * d, (int)M, 3 * d / gemm::BN, d, 0, gemm::BN / 2, gemm::BN, qkv_out, 3 * d,
-                      3 * d, epi, as_stream(stream));
+  return gemm::launch(x, in_features, w_qkv, in_features, 3 * d, (int)M, 3 * d / gemm::BN, in_features, 0,
+                      gemm::BN / 2, gemm::BN, qkv_out, 3 * d, 3 * d, epi, as_stream(stream));
 }
 
 extern "C" int engpt_up_gate_swiglu(const void* x, const void* w_ug, const float* s_u, const float* s_gate,

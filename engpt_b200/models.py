@@ -5,26 +5,29 @@ initialisation follow engpt/models.py:111-391, so ``state_dict`` keys match
 the reference and ``torch.manual_seed(s); EfficientNGPT(cfg)`` produces the
 reference's weights bit-for-bit (the init runs on the CPU with the same
 random draws).  ``forward`` / ``forward_carried`` run the carried-radius
-forward (engpt/models.py:263-292) on the GPU:
+forward (engpt/models.py:263-292) on the GPU; under bf16 autocast:
 
   per block (engpt/models.py:140-182)
-    q, k, v  = post-process(Y_bf16 @ W_qkv^T)            engpt_qkv_projection (tcgen05 GEMM, fused epilogue;
-                                                         otherwise cuBLAS + engpt_qkv_postprocess in place)
-    attn     = causal attention  -> [B,T,H,Dh]           engpt_causal_attention (tcgen05)
+    q, k, v  = post-process(Y_bf16 @ W_qkv^T)            engpt_qkv_projection (tcgen05 GEMM, post-process in
+                                                         the epilogue; head_dim 64 / 128)
+    attn     = causal attention  -> [B,T,H,Dh]           engpt_ngpt_attention (tcgen05, softmax offset from the
+                                                         s_qk score bound)
     branch   = attn @ W_o^T                              cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y/rho engpt_carried_residual_gauge
-    hidden   = SwiGLU((Y/rho)_bf16 @ W_ug^T)             engpt_up_gate_swiglu (tcgen05 GEMM, fused epilogue;
-                                                         fp32 mode: cuBLAS + engpt_swiglu)
+    hidden   = SwiGLU((Y/rho)_bf16 @ W_ug^T)             engpt_up_gate_swiglu (tcgen05 GEMM, SwiGLU epilogue)
     branch   = hidden @ W_down^T                         cuBLAS
     Y, rho   = carried residual + gauge, emits bf16 Y    engpt_carried_residual_gauge
-  logits = (Y/rho)_bf16 @ (E_out * s_z_eff)^T_bf16       engpt_scale_rows_cast + cuBLAS
-  loss   = mean token cross-entropy                      engpt_cross_entropy
+  logits, loss = head GEMM with the log-sum-exp          engpt_logits_cross_entropy (tcgen05 GEMM + merge;
+                 per 256-column tile in its epilogue     without targets: cuBLAS logits)
 
-Precision follows the reference's: under ``torch.autocast("cuda",
-torch.bfloat16)`` the carried state ``Y, rho`` stays fp32, GEMM operands and
-outputs, Q/K/V, attention output and logits are bf16, and the loss is fp32;
-outside autocast everything is fp32.  All activations live in a per-shape
-workspace that is reused across calls; returned logits and loss are fresh.
+Outside autocast (fp32 mode) the projections are fp32 cuBLAS GEMMs, the
+attention the fp32 CUDA-core kernel and SwiGLU / cross-entropy their own
+kernels.  Precision follows the reference's: under autocast the carried
+state ``Y, rho`` stays fp32, GEMM operands and outputs, Q/K/V, attention
+output and logits are bf16, and the loss is fp32.  All activations live in a
+per-shape workspace that is reused across calls; returned logits and loss
+are fresh.  ``set_head_split`` runs the forward as one rank of a group that
+shares each sequence's heads and MLP units (``engpt_b200.head_split``).
 """
 
 from __future__ import annotations
@@ -39,6 +42,7 @@ from torch import Tensor, nn
 from . import _lib
 from . import kernels as K
 from .config import ModelConfig
+from .head_split import HeadSplit
 
 
 def _ngpt_base_scale(cfg: ModelConfig) -> float:
@@ -134,22 +138,27 @@ class _Workspace:
     """Activation buffers for one (batch, seq_len, precision) shape on one device."""
 
     def __init__(self, cfg: ModelConfig, bsz: int, seq_len: int, device: torch.device, bf16: bool,
-                 fuse_mlp: bool = True):
-        d, H, Dh, W = cfg.n_embd, cfg.n_head, cfg.head_dim, cfg.mlp_width
+                 fuse_mlp: bool = True, split: Optional[HeadSplit] = None):
+        d, Dh, W_full = cfg.n_embd, cfg.head_dim, cfg.mlp_width
+        # with a head split this rank's heads and MLP units; the carried state stays full width
+        H = cfg.n_head // (split.size if split else 1)
+        W = W_full // (split.size if split else 1)
+        dl = H * Dh                           # width of this rank's heads
         n = bsz * seq_len
         act = torch.bfloat16 if bf16 else torch.float32
         e = lambda *shape, dtype=act: torch.empty(*shape, device=device, dtype=dtype)  # noqa: E731
-        self.key = (bsz, seq_len, bf16, device, fuse_mlp)
+        self.key = (bsz, seq_len, bf16, device, fuse_mlp, split.key() if split else None)
+        self.H, self.W, self.dl = H, W, dl
         self.bsz, self.seq_len, self.n = bsz, seq_len, n
         self.act = act
         self.y = e(n, d, dtype=torch.float32)
         self.rho = e(n, dtype=torch.float32)
         self.x = e(n, d)                      # GEMM operand: Y (QKV) or Y/rho (up/gate, head)
         # raw projection [B, T, 3, H, Dh]; the epilogue turns it into q, k, v in place
-        self.qkv = e(n, 3 * d)
+        self.qkv = e(n, 3 * dl)
         qkv5 = self.qkv.view(bsz, seq_len, 3, H, Dh)
         self.q, self.k, self.v = qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2]   # [B, T, H, Dh] views
-        self.attn = e(n, d)                   # [B, T, H, Dh]
+        self.attn = e(n, dl)                  # [B, T, H, Dh]
         self.branch = e(n, d)
         # bf16 mode fuses SwiGLU into the up/gate GEMM (no [n, 2W] buffer); fp32 mode runs cuBLAS + the
         # SwiGLU kernel
@@ -160,9 +169,11 @@ class _Workspace:
         self.sin = e(seq_len, Dh // 2, dtype=torch.float32)
         self.attn_strides = K.attention_strides(self.q, self.k, self.v, self.attn.view(bsz, seq_len, H, Dh),
                                                 head_major=False)
-        # bf16 weight copies (re-cast from the fp32 parameters on every forward)
+        # bf16 weight copies (re-cast from the fp32 parameters on every forward); with a head split the QKV
+        # and up/gate copies hold this rank's rows only, out_proj and down_proj are used through column views
         if bf16:
-            self.w = [dict(qkv=e(3 * d, d), out=e(d, d), ug=e(2 * W, d), down=e(d, W)) for _ in range(cfg.n_layer)]
+            self.w = [dict(qkv=e(3 * dl, d), out=e(d, d), ug=e(2 * W, d), down=e(d, W_full))
+                      for _ in range(cfg.n_layer)]
         else:
             self.w = None
         # output-head weight with the vocab rounded up to a multiple of 64 rows (pad rows stay zero):
@@ -216,6 +227,8 @@ class EfficientNGPT(nn.Module):
         self.contiguous_logits = False
         # optional instrumentation: called around the attention launch of every layer
         self.attn_timer: Optional[Callable[[str], None]] = None
+        # this rank's share of a head-split group (set_head_split), or None for the whole model
+        self.head_split: Optional[HeadSplit] = None
 
     def _init_weights(self, module: nn.Module) -> None:
         if isinstance(module, (nn.Linear, nn.Embedding)):
@@ -285,11 +298,27 @@ class EfficientNGPT(nn.Module):
         return loss
 
     def _workspace(self, bsz: int, seq_len: int, device: torch.device, bf16: bool) -> _Workspace:
-        key = (bsz, seq_len, bf16, device, self.fuse_mlp)
+        split = self.head_split
+        key = (bsz, seq_len, bf16, device, self.fuse_mlp, split.key() if split else None)
         if self._ws is None or self._ws.key != key:
             self._ws = None
-            self._ws = _Workspace(self.cfg, bsz, seq_len, device, bf16, self.fuse_mlp)
+            self._ws = _Workspace(self.cfg, bsz, seq_len, device, bf16, self.fuse_mlp, split)
         return self._ws
+
+    def set_head_split(self, split: Optional[HeadSplit]) -> None:
+        """Run the forward as one rank of a head-split group (``engpt_b200.head_split``), or whole (None).
+
+        Every rank of the group holds the full weights and calls ``forward`` on the
+        same ids; each computes its heads and MLP units, and the partial branches are
+        summed over the group before every carried residual, so all ranks return the
+        same logits and loss.
+        """
+        if split is not None:
+            split.validate(self.cfg.n_head, self.cfg.mlp_width)
+            if split.size == 1:
+                split = None
+        self.head_split = split
+        self._ws = None
 
     def release_workspace(self) -> None:
         self._ws = None
@@ -319,6 +348,11 @@ class EfficientNGPT(nn.Module):
         bsz, seq_len = src.shape[0], src.shape[1]
         n = bsz * seq_len
         d, H, Dh, W = cfg.n_embd, cfg.n_head, cfg.head_dim, cfg.mlp_width
+        # head split (engpt_b200.head_split): this rank's heads [h0, h1) and MLP units [u0, u1)
+        split = self.head_split
+        h0, h1 = split.heads(H) if split else (0, H)
+        u0, u1 = split.units(W) if split else (0, W)
+        Hl, dl, Wl = h1 - h0, (h1 - h0) * Dh, u1 - u0
         ws = self._workspace(bsz, seq_len, dev, bf16)
         st = _lib.stream_handle(dev)
         act = _lib.dtype_code(ws.act)
@@ -342,13 +376,25 @@ class EfficientNGPT(nn.Module):
             if bf16:
                 # autocast's per-forward bf16 copies of the linear weights, in one batched launch
                 srcs, dsts, counts = [], [], []
+
+                def add(src, src_row, dst, dst_row, nrows):   # rows [src_row, +nrows) of an fp32 [., d] matrix
+                    cols = src.shape[1]
+                    srcs.append(src.data_ptr() + 4 * src_row * cols)
+                    dsts.append(dst.data_ptr() + 2 * dst_row * cols)
+                    counts.append(nrows * cols)
+
                 for i, blk in enumerate(self.blocks):
                     w = ws.w[i]
-                    for name, p in (("qkv", blk.qkv.weight), ("out", blk.out_proj.weight),
-                                    ("ug", blk.up_gate.weight), ("down", blk.down_proj.weight)):
-                        srcs.append(p.data_ptr())
-                        dsts.append(w[name].data_ptr())
-                        counts.append(p.numel())
+                    if split is None:
+                        add(blk.qkv.weight, 0, w["qkv"], 0, 3 * d)
+                        add(blk.up_gate.weight, 0, w["ug"], 0, 2 * W)
+                    else:   # this rank's q, k and v rows; its u and gate rows
+                        for part in range(3):
+                            add(blk.qkv.weight, part * d + h0 * Dh, w["qkv"], part * dl, dl)
+                        add(blk.up_gate.weight, u0, w["ug"], 0, Wl)
+                        add(blk.up_gate.weight, W + u0, w["ug"], Wl, Wl)
+                    add(blk.out_proj.weight, 0, w["out"], 0, d)
+                    add(blk.down_proj.weight, 0, w["down"], 0, d)
                 nw = len(srcs)
                 _lib.call("engpt_cast_f32_bf16_many", (ctypes.c_void_p * nw)(*srcs), (ctypes.c_void_p * nw)(*dsts),
                           (ctypes.c_int64 * nw)(*counts), nw, st)
@@ -363,17 +409,25 @@ class EfficientNGPT(nn.Module):
                 else:
                     wq, wo, wug, wd = blk.qkv.weight, blk.out_proj.weight, blk.up_gate.weight, blk.down_proj.weight
                     x_in = ws.y
-                if bf16 and self.fuse_qkv and Dh in (64, 128) and d % 256 == 0:
+                    if split is not None:   # this rank's q, k, v rows and u, gate rows (fp32 mode copies them)
+                        wq = torch.cat([wq[p * d + h0 * Dh:p * d + h1 * Dh] for p in range(3)])
+                        wug = torch.cat([wug[u0:u1], wug[W + u0:W + u1]])
+                # this rank's columns of out_proj / down_proj, its heads' s_qk rows and its units' scales
+                wo_r = wo[:, h0 * Dh:h1 * Dh] if split else wo
+                wd_r = wd[:, u0:u1] if split else wd
+                s_qk = blk.s_qk[h0:h1]
+                s_u, s_gate = blk.s_u[u0:u1], blk.s_gate[u0:u1]
+                if bf16 and self.fuse_qkv and Dh in (64, 128) and dl % 256 == 0:
                     # QKV GEMM with the post-process fused into its epilogue (tcgen05): q|k|v rows are
                     # written post-processed into the same [n, 3, H, Dh] buffer
-                    _lib.call("engpt_qkv_projection", x_in.data_ptr(), wq.data_ptr(), ws.rho.data_ptr(),
-                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(),
-                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, H, Dh, ws.qkv.data_ptr(), st)
+                    _lib.call("engpt_qkv_projection", x_in.data_ptr(), d, wq.data_ptr(), ws.rho.data_ptr(),
+                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, s_qk.data_ptr(),
+                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, Hl, Dh, ws.qkv.data_ptr(), st)
                 else:
                     torch.mm(x_in, wq.t(), out=ws.qkv)
                     _lib.call("engpt_qkv_postprocess", ws.qkv.data_ptr(), act, ws.rho.data_ptr(),
-                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, blk.s_qk.data_ptr(),
-                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, H, Dh, None, None, None,
+                              ws.cos.data_ptr(), ws.sin.data_ptr(), Dh // 2, s_qk.data_ptr(),
+                              float(blk.qk_mult), float(cfg.norm_eps), bsz, seq_len, Hl, Dh, None, None, None,
                               _lib.QKV_INPLACE, st)
                 if self.attn_timer is not None:
                     self.attn_timer("start")
@@ -381,15 +435,15 @@ class EfficientNGPT(nn.Module):
                     # q, k are unit vectors times the effective s_qk (the post-process above): the kernel takes
                     # its softmax offset from the per-head score bound max_i s_qk[h, i]^2 (no running max)
                     _lib.call("engpt_ngpt_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
-                              ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
-                              blk.s_qk.data_ptr(), float(blk.qk_mult), st)
+                              ws.attn.data_ptr(), act, bsz, seq_len, Hl, Dh, float(scale),
+                              ws.attn_strides.data_ptr(), s_qk.data_ptr(), float(blk.qk_mult), st)
                 else:
                     _lib.call("engpt_causal_attention", ws.q.data_ptr(), ws.k.data_ptr(), ws.v.data_ptr(),
-                              ws.attn.data_ptr(), act, bsz, seq_len, H, Dh, float(scale), ws.attn_strides.data_ptr(),
-                              self.attn_impl, st)
+                              ws.attn.data_ptr(), act, bsz, seq_len, Hl, Dh, float(scale),
+                              ws.attn_strides.data_ptr(), self.attn_impl, st)
                 if self.attn_timer is not None:
                     self.attn_timer("stop")
-                fuse_res = bf16 and self.fuse_residual and d % 256 == 0 and d <= 1024
+                fuse_res = bf16 and self.fuse_residual and d % 256 == 0 and d <= 1024 and split is None
                 if fuse_res:
                     # out_proj GEMM with the carried residual in its epilogue (tcgen05, d/256-CTA clusters):
                     # the branch never leaves the chip
@@ -399,7 +453,9 @@ class EfficientNGPT(nn.Module):
                               float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(), ws.rho.data_ptr(),
                               ws.x.data_ptr(), _lib.AUX_BF16_H, st)
                 else:
-                    torch.mm(ws.attn, wo.t(), out=ws.branch)
+                    torch.mm(ws.attn, wo_r.t(), out=ws.branch)
+                    if split is not None:   # the heads' partial branches summed over the group
+                        split.all_reduce_(ws.branch)
                     _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(),
                               ws.branch.data_ptr(), act, blk.alpha_attn_raw.data_ptr(), float(blk.alpha_mult), 1,
                               float(cfg.norm_eps), float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d,
@@ -408,13 +464,13 @@ class EfficientNGPT(nn.Module):
                 if ws.ug is None:
                     # up/gate GEMM with the SwiGLU epilogue fused (tcgen05): the [n, 2W] projection never
                     # leaves TMEM
-                    _lib.call("engpt_up_gate_swiglu", ws.x.data_ptr(), wug.data_ptr(), blk.s_u.data_ptr(),
-                              blk.s_gate.data_ptr(), float(u_mult), float(sqrt_d), n, d, W,
+                    _lib.call("engpt_up_gate_swiglu", ws.x.data_ptr(), wug.data_ptr(), s_u.data_ptr(),
+                              s_gate.data_ptr(), float(u_mult), float(sqrt_d), n, d, Wl,
                               ws.hidden.data_ptr(), st)
                 else:
                     torch.mm(ws.x, wug.t(), out=ws.ug)
-                    _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, blk.s_u.data_ptr(), blk.s_gate.data_ptr(),
-                              float(u_mult), float(sqrt_d), n, W, ws.hidden.data_ptr(), act, st)
+                    _lib.call("engpt_swiglu", ws.ug.data_ptr(), act, s_u.data_ptr(), s_gate.data_ptr(),
+                              float(u_mult), float(sqrt_d), n, Wl, ws.hidden.data_ptr(), act, st)
                 if i < last:
                     aux_mode = _lib.AUX_BF16_Y if bf16 else _lib.AUX_NONE
                 else:
@@ -426,7 +482,9 @@ class EfficientNGPT(nn.Module):
                               float(cfg.carried_gauge_max), n, d, ws.y.data_ptr(), ws.rho.data_ptr(),
                               ws.x.data_ptr(), aux_mode, st)
                 else:
-                    torch.mm(ws.hidden, wd.t(), out=ws.branch)
+                    torch.mm(ws.hidden, wd_r.t(), out=ws.branch)
+                    if split is not None:   # the units' partial branches summed over the group
+                        split.all_reduce_(ws.branch)
                     _lib.call("engpt_carried_residual_gauge", ws.y.data_ptr(), ws.rho.data_ptr(),
                               ws.branch.data_ptr(), act, blk.alpha_mlp_raw.data_ptr(), float(blk.alpha_mult), 1,
                               float(cfg.norm_eps), float(cfg.norm_eps), float(cfg.carried_gauge_max), n, d,

@@ -214,14 +214,18 @@ ENGPT_API int engpt_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t
 /*
  * QKV projection with the QKV post-process fused into the GEMM epilogue --
  * F.linear of engpt/models.py:142 followed by qkv_postprocess_from_carried
- * (engpt/kernels.py:139-179) on the fp32 accumulator: x [B*T, d] bf16,
- * w_qkv [3d, d] bf16; writes the post-processed q | k | v rows into qkv_out
- * [B*T, 3, H, Dh] bf16 (the layout engpt_qkv_postprocess leaves in place).
- * head_dim 64 or 128, d a multiple of 256.
+ * (engpt/kernels.py:139-179) on the fp32 accumulator: x [B*T, in_features]
+ * bf16, w_qkv [3 * H * Dh, in_features] bf16 (the q rows of the H heads, then
+ * their k rows, then their v rows; in_features = H * Dh for the whole model,
+ * the model width for a head group of a head split); writes the
+ * post-processed q | k | v rows into qkv_out [B*T, 3, H, Dh] bf16 (the layout
+ * engpt_qkv_postprocess leaves in place).  head_dim 64 or 128, H * Dh a
+ * multiple of 256, in_features a multiple of 8.
  */
-ENGPT_API int engpt_qkv_projection(const void* x, const void* w_qkv, const float* rho, const float* cos_tab,
-                                   const float* sin_tab, int rope_half, const float* qk_scale, float qk_mult,
-                                   float norm_eps, int B, int T, int H, int Dh, void* qkv_out, void* stream);
+ENGPT_API int engpt_qkv_projection(const void* x, int in_features, const void* w_qkv, const float* rho,
+                                   const float* cos_tab, const float* sin_tab, int rope_half, const float* qk_scale,
+                                   float qk_mult, float norm_eps, int B, int T, int H, int Dh, void* qkv_out,
+                                   void* stream);
 
 /*
  * Up/gate projection with SwiGLU fused into the GEMM epilogue --

@@ -35,7 +35,7 @@ def test_binding_covers_every_declared_symbol():
 
 def test_host_side_validation_without_gpu():
     lib = _lib.load()
-    assert lib.engpt_abi_version() == 100
+    assert lib.engpt_abi_version() == 101
     # argument checks run on the host before any CUDA call
     rc = lib.engpt_carried_residual_gauge(None, None, None, 1, None, 1.0, 0, 0.0, 0.0, 0.0, 4, 8, None, None,
                                           None, 0, None)

@@ -466,7 +466,7 @@ def test_qkv_projection_matches_unfused_path(cuda, B, T):
     cos, sin = K.rotary_frequencies(T, Dh, device=cuda, dtype=torch.float32, theta=10000.0)
     qks = (torch.rand(H, Dh, generator=g) + 0.5).to(cuda)
     fused = torch.empty(n, 3 * d, device=cuda, dtype=torch.bfloat16)
-    _lib.call("engpt_qkv_projection", x.data_ptr(), w.data_ptr(), rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+    _lib.call("engpt_qkv_projection", x.data_ptr(), d, w.data_ptr(), rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
               Dh // 2, qks.data_ptr(), 2.0, 1e-6, B, T, H, Dh, fused.data_ptr(), _stream())
     unf = torch.mm(x, w.t())
     _lib.call("engpt_qkv_postprocess", unf.data_ptr(), _lib.BF16, rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
@@ -490,7 +490,7 @@ def test_qkv_projection_vs_oracle_d1024(cuda, B, T, H, Dh):
     s_qk = (torch.rand(H, Dh, generator=g) * 0.2 + 0.9) / 32.0      # raw parameter; x 32 = effective
     s_qk = s_qk.to(cuda)
     out = torch.empty(n, 3 * d, device=cuda, dtype=torch.bfloat16)
-    _lib.call("engpt_qkv_projection", x.data_ptr(), w.data_ptr(), rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+    _lib.call("engpt_qkv_projection", x.data_ptr(), d, w.data_ptr(), rho.data_ptr(), cos.data_ptr(), sin.data_ptr(),
               Dh // 2, s_qk.data_ptr(), 32.0, 1e-6, B, T, H, Dh, out.data_ptr(), _stream())
     x64 = x.double().cpu().numpy()
     w64 = w.double().cpu().numpy()
