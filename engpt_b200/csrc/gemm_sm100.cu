@@ -174,8 +174,27 @@ struct QkvEpi {
         load_acc32(th + 64 * half, x);
         load_acc32(th + 64 * half + 32, x + 32);
         const int p0 = 32 * half;                                   // first rotary pair of this half
-        const float* crow = cos_tab + (int64_t)t * rope_half;
-        const float* srow = sin_tab + (int64_t)t * rope_half;
+        // this half's 32 rotary pairs: vector loads issued together (pairs >= rope_half: cos 1, sin 0)
+        float cs[32], sn[32];
+        {
+          const float* crow = cos_tab + (int64_t)t * rope_half + p0;
+          const float* srow = sin_tab + (int64_t)t * rope_half + p0;
+          if (rope_half == 64) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 c4 = __ldg(reinterpret_cast<const float4*>(crow + i));
+              const float4 s4 = __ldg(reinterpret_cast<const float4*>(srow + i));
+              cs[i] = c4.x; cs[i + 1] = c4.y; cs[i + 2] = c4.z; cs[i + 3] = c4.w;
+              sn[i] = s4.x; sn[i + 1] = s4.y; sn[i + 2] = s4.z; sn[i + 3] = s4.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              cs[i] = p0 + i < rope_half ? __ldg(crow + i) : 1.f;
+              sn[i] = p0 + i < rope_half ? __ldg(srow + i) : 0.f;
+            }
+          }
+        }
         uint4 o[8];
 #pragma unroll
         for (int i = 0; i < 64; i += 8) {
@@ -185,12 +204,10 @@ struct QkvEpi {
           float v[8];
 #pragma unroll
           for (int k = 0; k < 8; k += 2) {
-            const int pi = p0 + ((i + k) >> 1);
-            const float c = pi < rope_half ? __ldg(crow + pi) : 1.f;
-            const float sn = pi < rope_half ? __ldg(srow + pi) : 0.f;
+            const int pi = (i + k) >> 1;
             const float xe = x[i + k], xo = x[i + k + 1];
-            v[k] = ((xe * c - xo * sn) * f) * scl[k];
-            v[k + 1] = ((xe * sn + xo * c) * f) * scl[k + 1];
+            v[k] = ((xe * cs[pi] - xo * sn[pi]) * f) * scl[k];
+            v[k + 1] = ((xe * sn[pi] + xo * cs[pi]) * f) * scl[k + 1];
           }
           o[i / 8] = pack8(v);
         }
