@@ -521,6 +521,11 @@ def reference_gpu_timing(a, dev, model):
                     ours(idx, tgt)
             ms = _time_forward(run_ours, 3, 5)
             rec.update({"engpt_b200_tok_s": batch * seq / (ms / 1000.0), "engpt_b200_ms": ms})
+            # the same forward replayed from a CUDA graph (model.enable_cuda_graphs): no per-kernel host launches
+            ours.enable_cuda_graphs()
+            ms = _time_forward(run_ours, 3, 20)
+            ours.enable_cuda_graphs(False)
+            rec.update({"engpt_b200_cuda_graph_tok_s": batch * seq / (ms / 1000.0), "engpt_b200_cuda_graph_ms": ms})
         torch.cuda.empty_cache()
         return rec
 

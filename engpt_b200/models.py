@@ -192,6 +192,34 @@ class _Workspace:
         return self._lse
 
 
+class _GraphedForward:
+    """One captured forward: static id / target buffers on the device, the graph, and its output buffers.
+
+    It keeps the workspace it was captured with alive (the graph holds raw
+    pointers into it), whatever the model's current workspace becomes.
+    """
+
+    def __init__(self, model: "EfficientNGPT", shape: tuple, has_targets: bool, dev: torch.device) -> None:
+        self.idx = torch.zeros(shape, dtype=torch.int64, device=dev)
+        self.targets = torch.zeros(shape, dtype=torch.int64, device=dev) if has_targets else None
+        self.graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            model._run(idx=self.idx, targets=self.targets)   # warm-up: workspace, tensor maps, library handles
+        torch.cuda.current_stream(dev).wait_stream(side)
+        with torch.cuda.graph(self.graph):
+            self.logits, self.loss = model._run(idx=self.idx, targets=self.targets)
+        self.ws = model._ws
+
+    def replay(self, idx: Tensor, targets: Optional[Tensor]) -> Tuple[Tensor, Optional[Tensor]]:
+        self.idx.copy_(idx, non_blocking=True)
+        if targets is not None:
+            self.targets.copy_(targets, non_blocking=True)
+        self.graph.replay()
+        return self.logits, self.loss
+
+
 class EfficientNGPT(nn.Module):
     """Carried-radius nGPT (engpt/models.py:233-391) with a fused B200 forward."""
 
@@ -229,6 +257,10 @@ class EfficientNGPT(nn.Module):
         self.attn_timer: Optional[Callable[[str], None]] = None
         # this rank's share of a head-split group (set_head_split), or None for the whole model
         self.head_split: Optional[HeadSplit] = None
+        # forward(idx, targets) replays one CUDA graph per input shape (captured on first use) instead of
+        # launching ~10 kernels per layer from Python; see enable_cuda_graphs
+        self.cuda_graphs = False
+        self._graphs: Dict[tuple, "_GraphedForward"] = {}
 
     def _init_weights(self, module: nn.Module) -> None:
         if isinstance(module, (nn.Linear, nn.Embedding)):
@@ -265,7 +297,48 @@ class EfficientNGPT(nn.Module):
         self._check_inference()
         if idx.size(1) > self.cfg.block_size:
             raise ValueError("sequence length exceeds block_size")
+        if self.cuda_graphs and self.head_split is None:
+            return self._graphed(idx, targets)
         return self._run(idx=idx, targets=targets)
+
+    # ---------------------------------------------------------------- CUDA graphs
+    def enable_cuda_graphs(self, enabled: bool = True) -> None:
+        """Replay ``forward(idx, targets)`` from CUDA graphs, one per (batch, sequence, targets, autocast) key.
+
+        The first call with a key runs the forward once eagerly (warm-up) and
+        captures a second run; later calls copy ``idx`` / ``targets`` into the
+        graph's input buffers and replay it.  The graph reads the parameters in
+        place, so in-place updates (an optimizer step, ``load_state_dict``) are
+        seen; parameters moved to new storage (``.to()`` of another device or
+        dtype, reassigned tensors) need ``reset_cuda_graphs()``.  The returned
+        ``logits`` and ``loss`` are the graph's output buffers: the next replay of
+        the same key overwrites them (clone to keep them).  A head-split model
+        runs eagerly (its all-reduces go through the process group).
+        """
+        self.cuda_graphs = enabled
+        if not enabled:
+            self.reset_cuda_graphs()
+
+    def reset_cuda_graphs(self) -> None:
+        self._graphs.clear()
+
+    def _param_key(self) -> tuple:
+        return (self.token_emb.weight.data_ptr(), self.output_emb.data_ptr(), self.s_z.data_ptr(),
+                self.blocks[0].qkv.weight.data_ptr(), self.blocks[-1].down_proj.weight.data_ptr())
+
+    def _graphed(self, idx: Tensor, targets: Optional[Tensor]) -> Tuple[Tensor, Optional[Tensor]]:
+        dev = self.token_emb.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("engpt_b200 EfficientNGPT runs on CUDA only (no CPU fallback); call .cuda()")
+        if targets is not None and targets.shape != idx.shape:
+            raise NotImplementedError("engpt_b200 implements token targets [batch, sequence] only")
+        key = (tuple(idx.shape), targets is not None, self._mode_bf16(dev), dev, self.fuse_mlp, self.fuse_qkv,
+               self.fuse_residual, self.fuse_head, self.attn_impl, self.contiguous_logits, self._param_key())
+        g = self._graphs.get(key)
+        if g is None:
+            g = _GraphedForward(self, tuple(idx.shape), targets is not None, dev)
+            self._graphs[key] = g
+        return g.replay(idx, targets)
 
     def forward_carried(self, y: Tensor, rho: Tensor,
                         targets: Optional[Tensor] = None) -> Tuple[Tensor, Optional[Tensor]]:

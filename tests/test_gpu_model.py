@@ -243,3 +243,44 @@ def test_head_dim_128_bf16_tracks_fp32_engine(cuda):
         hf = (yf / rf.unsqueeze(-1)).reshape(-1, 256).cpu().numpy()
         assert row_rel_err(hb, hf) < BF16_TOL
     assert abs(loss_b.item() - loss_f.item()) < 2e-2
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_cuda_graph_replay_matches_eager(cuda, bf16):
+    """enable_cuda_graphs(): the captured forward, replayed for new ids and targets, gives exactly the eager
+    forward's logits and loss (the same kernels on the same inputs); an in-place parameter update is seen by the
+    next replay; a second shape gets its own graph."""
+    cfg = ModelConfig(vocab_size=1000, block_size=256, n_layer=3, n_head=4, n_embd=256, mlp_ratio=4.0, dropout=0.0)
+    torch.manual_seed(0)
+    model = EfficientNGPT(cfg).to(cuda).eval().requires_grad_(False)
+    gen = torch.Generator().manual_seed(5)
+    batches = [torch.randint(0, cfg.vocab_size, (2, 256), generator=gen) for _ in range(3)]
+
+    def run(idx):
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
+            logits, loss = model(idx.to(cuda), torch.roll(idx, -1, dims=1).to(cuda))
+        return logits.float().clone(), loss.clone()
+
+    eager = [run(b) for b in batches]
+    model.enable_cuda_graphs()
+    graphed = [run(b) for b in batches] + [run(batches[0])]
+    for (le, lo), (lg, log) in zip(eager + eager[:1], graphed):
+        assert torch.equal(le, lg)
+        assert torch.equal(lo, log)
+    with torch.no_grad():
+        model.s_z.mul_(1.5)               # in place: the captured graph reads the new values
+    got = run(batches[1])
+    model.enable_cuda_graphs(False)
+    want = run(batches[1])
+    assert not torch.equal(want[0], eager[1][0])
+    assert torch.equal(want[0], got[0]) and torch.equal(want[1], got[1])
+    model.enable_cuda_graphs()
+    run(batches[2])                       # captured again (disabling dropped the graphs)
+    short = torch.randint(0, cfg.vocab_size, (1, 128), generator=gen)
+    model.enable_cuda_graphs(False)
+    want = run(short)
+    model.enable_cuda_graphs()
+    run(batches[0])
+    got = run(short)
+    assert torch.equal(want[0], got[0]) and torch.equal(want[1], got[1])
+    assert len(model._graphs) == 2
