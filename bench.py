@@ -103,6 +103,8 @@ def parse_args():
                          "MLP units (two all-reduces per layer); the batch is split over the groups")
     ap.add_argument("--gather", choices=["hidden", "logits", "none"], default="hidden",
                     help="N>1: outputs all-gathered over NCCL inside the timed step (final Y/rho, or the logits)")
+    ap.add_argument("--cuda-graph", choices=["on", "off"], default="off",
+                    help="replay the forward from a CUDA graph (EfficientNGPT.enable_cuda_graphs)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
@@ -349,7 +351,20 @@ def run_gpu(a, world, rank, local_rank):
                 out = sharding.gather_rows(logits, global_batch, group=dp_group)
         return out, loss
 
+    graphs = a.cuda_graph == "on"
+    if graphs:
+        model.enable_cuda_graphs()
     for _ in range(max(a.warmup, 1)):
+        step(idx_d, tgt_d)
+    torch.cuda.synchronize()
+    # kernels of one forward (a graph replays the launches counted while it was captured)
+    counter["n"] = 0
+    if graphs:
+        model.enable_cuda_graphs(False)
+    step(idx_d, tgt_d)
+    per_forward = counter["n"]
+    if graphs:
+        model.enable_cuda_graphs()
         step(idx_d, tgt_d)
     torch.cuda.synchronize()
 
@@ -377,10 +392,17 @@ def run_gpu(a, world, rank, local_rank):
         del out
     ev1.record()
     torch.cuda.synchronize()
-    launches = counter["n"]
+    launches = counter["n"] if not graphs else per_forward * a.steps
     if world > 1:
         dist.barrier()
     clocks = sampler.stop() if sampler else None
+    if graphs:
+        # a replayed graph runs no Python hooks: the attention launches are timed in one eager step after the
+        # timed region (same inputs, same kernels)
+        model.enable_cuda_graphs(False)
+        step(idx_d, tgt_d)
+        torch.cuda.synchronize()
+        model.enable_cuda_graphs()
     model.attn_timer = None
     ms = ev0.elapsed_time(ev1)
     attn_ms = [attn_events[i].elapsed_time(attn_events[i + 1]) for i in range(0, len(attn_events), 2)]
@@ -433,7 +455,7 @@ def run_gpu(a, world, rank, local_rank):
         "metric": metric_name(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform random ids, seeded random-init unit-sphere weights)",
-        "config": workload_config(a, world),
+        "config": {**workload_config(a, world), "cuda_graph": a.cuda_graph},
         "e2e": {"value": e2e, "unit": UNIT,
                 "h2d_bytes_per_step": 2 * global_batch * hs * a.seq * idx_h.element_size(),
                 "d2h_bytes_per_step": 4 * world},
