@@ -180,13 +180,14 @@ def test_attention_tcgen05_bf16_vs_oracle(cuda, D, T):
     assert err <= 2.0 * err_torch + 2e-3, (err, err_torch)
 
 
-@pytest.mark.parametrize("B,T,H", [(8, 1152, 16), (8, 1200, 16), (2, 2048, 16)])
+@pytest.mark.parametrize("B,T,H", [(8, 1152, 16), (8, 1200, 16), (2, 2048, 16), (20, 2048, 16)])
 def test_attention_tcgen05_many_bands_per_cta(cuda, B, T, H):
     """More 256-query bands than SMs, so every CTA of the persistent head_dim-64 kernel walks several bands:
     the Q double buffer, the job / K-V / PV counters that run across bands, the band store deferred past the
     next band's first job, last bands whose second 128-row tile is empty (T = 1152: T mod 256 = 128) or only
-    partly filled (T = 1200: T mod 256 = 176).  Reference: torch's fp32 causal SDPA on the same bf16-rounded
-    inputs; bound as in the oracle test above."""
+    partly filled (T = 1200: T mod 256 = 176).  The first three take the bands by size class (their K/V fit
+    in L2), B=20 by (batch, head).  Reference: torch's fp32 causal SDPA on the same bf16-rounded inputs;
+    bound as in the oracle test above."""
     D = 64
     q, k, v = _attn_inputs(B, T, H, D, seed=B * T + H)
     qb, kb, vb = (x.to(cuda, torch.bfloat16) for x in (q, k, v))
