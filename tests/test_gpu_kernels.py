@@ -104,11 +104,13 @@ def test_carried_residual_gauge_fp32_matches_reference(golden, cuda, tag, max_ra
     np.testing.assert_allclose(r.cpu().numpy(), g[f"res_{tag}_rho"], rtol=2e-6, atol=2e-6)
 
 
-@pytest.mark.parametrize("d", [32, 100, 256, 1024, 2048, 4096])
+@pytest.mark.parametrize("d,rows", [(32, 77), (100, 77), (256, 77), (1024, 77), (2048, 77), (4096, 77),
+                                    (256, 20000), (1024, 20000), (2048, 20000)])
 @pytest.mark.parametrize("bdtype", [torch.float32, torch.bfloat16])
-def test_carried_residual_aux_outputs_and_in_place(cuda, d, bdtype):
-    rng = np.random.default_rng(d)
-    rows = 77
+def test_carried_residual_aux_outputs_and_in_place(cuda, d, rows, bdtype):
+    """Against the oracle, in place, every aux mode.  77 rows take the four-warps-per-row kernel (d a multiple of
+    8, up to 2048) or the generic one; 20000 rows the one-warp-per-row kernel."""
+    rng = np.random.default_rng(d + rows)
     y = rng.standard_normal((rows, d)) * 40.0
     rho = rng.uniform(1.0, 1000.0, rows)
     branch = rng.standard_normal((rows, d))
