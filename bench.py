@@ -103,6 +103,9 @@ def parse_args():
                          "MLP units (two all-reduces per layer); the batch is split over the groups")
     ap.add_argument("--gather", choices=["hidden", "logits", "none"], default="hidden",
                     help="N>1: outputs all-gathered over NCCL inside the timed step (final Y/rho, or the logits)")
+    ap.add_argument("--overlap-collectives", choices=["on", "off"], default="on",
+                    help="N>1: run each step's loss all-reduce and output all-gather on NCCL's stream during the next "
+                         "step's forward (equal shards, no head split)")
     ap.add_argument("--cuda-graph", choices=["on", "off"], default="off",
                     help="replay the forward from a CUDA graph (EfficientNGPT.enable_cuda_graphs)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
@@ -126,7 +129,10 @@ def workload_config(a, world):
                          f"dp{world}: the batch split by sequences over the ranks, no collective inside the forward")
                         + f" ({a.scaling} scaling)"
                         + (f"; per step one all-reduce of the loss and an all-gather of the {a.gather} outputs"
-                           if world > 1 and a.gather != "none" else "")),
+                           if world > 1 and a.gather != "none" else "")
+                        + ("; the step's collectives overlap the next step's forward (NCCL stream)"
+                           if world > 1 and getattr(a, "overlap_collectives", "off") == "on" and hs == 1
+                           and a.gather != "logits" and gb % (world // hs) == 0 else "")),
         "l2": "no flush: activations per step (~10 GB at 32 sequences) exceed the 126 MB L2",
     }
 
@@ -337,10 +343,50 @@ def run_gpu(a, world, rank, local_rank):
     # this shard's counted targets (device scalar); a head-split group counts its sequences once
     n_valid = sharding.valid_targets(tgt_d) * (1 if rank % hs == 0 else 0)
 
+    # N > 1, batch shards of equal size, the final state gathered: the step's collectives (the loss all-reduce
+    # and the all-gather) run on NCCL's stream while the next step's forward runs.  Two buffer sets alternate;
+    # a set is rewritten only after the collectives of the step two back that used it completed.
+    overlap = (world > 1 and a.overlap_collectives == "on" and hs == 1 and a.gather in ("hidden", "none")
+               and global_batch % replicas == 0)
+    pend = {"slot": 0, "works": [[], []], "send": [None, None], "recv": [None, None], "part": [None, None]}
+    side = torch.cuda.Stream(dev)
+
+    def submit(loss):
+        b = pend["slot"] & 1
+        pend["slot"] += 1
+        for w in pend["works"][b]:
+            w.wait()
+        torch.cuda.current_stream(dev).wait_stream(side)   # the loss copy that read part[b] two steps back
+        nv = n_valid.to(device=dev, dtype=torch.float64)
+        part = torch.stack([torch.where(nv > 0, loss.to(torch.float64) * nv, 0.0), nv])
+        pend["part"][b] = part
+        works = [dist.all_reduce(part, op=dist.ReduceOp.SUM, async_op=True)]
+        if a.gather == "hidden":
+            hidden = model.last_hidden()
+            if pend["send"][b] is None:
+                pend["send"][b] = torch.empty_like(hidden)
+                pend["recv"][b] = hidden.new_empty((global_batch,) + tuple(hidden.shape[1:]))
+            pend["send"][b].copy_(hidden)   # the next forward rewrites the workspace
+            works.append(dist.all_gather_into_tensor(pend["recv"][b], pend["send"][b], group=dp_group,
+                                                     async_op=True))
+        pend["works"][b] = works
+        return pend["recv"][b], part
+
+    def drain():
+        for ws in pend["works"]:
+            for w in ws:
+                w.wait()
+        torch.cuda.current_stream(dev).wait_stream(side)
+
+    def part_loss(part):
+        return torch.where(part[1] > 0, part[0] / part[1], float("nan")).to(torch.float32)
+
     def step(idx, tgt):
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             logits, loss = model(idx, tgt)
         out = None
+        if overlap:
+            return submit(loss)
         if world > 1:
             # token-weighted mean over all shards (one all-reduce of 2 doubles), then the outputs of every
             # shard gathered over NCCL: the final represented state [B, T, d] bf16, or the logits
@@ -390,6 +436,9 @@ def run_gpu(a, world, rank, local_rank):
     for _ in range(a.steps):
         out, loss = step(idx_d, tgt_d)
         del out
+    if overlap:
+        drain()
+        loss = part_loss(loss)
     ev1.record()
     torch.cuda.synchronize()
     launches = counter["n"] if not graphs else per_forward * a.steps
@@ -413,6 +462,8 @@ def run_gpu(a, world, rank, local_rank):
     idx_p, tgt_p = idx_h.pin_memory(), tgt_h.pin_memory()
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     step(idx_p, tgt_p)
+    if overlap:
+        drain()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -420,7 +471,17 @@ def run_gpu(a, world, rank, local_rank):
     e0.record()
     for _ in range(a.steps):
         _, loss = step(idx_p, tgt_p)
-        loss_h.copy_(loss, non_blocking=True)
+        if overlap:
+            # the step's loss once its all-reduce completed, copied out on a side stream (the forward of the
+            # next step does not wait for it)
+            work = pend["works"][(pend["slot"] - 1) & 1][0]
+            with torch.cuda.stream(side):
+                work.wait()
+                loss_h.copy_(part_loss(loss), non_blocking=True)
+        else:
+            loss_h.copy_(loss, non_blocking=True)
+    if overlap:
+        drain()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

@@ -91,6 +91,11 @@ def gather_rows(local: Tensor, batch: int, *, group=None) -> Tensor:
     s, e = shard_range(batch, rank, world)
     if local.shape[0] != e - s:
         raise ValueError(f"rank {rank} holds {local.shape[0]} rows, its shard has {e - s}")
+    if batch % world == 0:
+        # equal shards: one collective straight into the output
+        out = local.new_empty((batch,) + tuple(local.shape[1:]))
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+        return out
     rows = -(-batch // world)  # largest shard
     buf = local.new_zeros((rows,) + tuple(local.shape[1:]))
     buf[: local.shape[0]].copy_(local)

@@ -75,8 +75,10 @@ def _worker(rank, world, port, weights, idx, targets, out_dir):
         # an empty shard on the last rank: loss only, no gather
         _, loss1 = sharding.forward_sharded(fwd, torch.from_numpy(idx[:1]), torch.from_numpy(targets[:1]),
                                             gather_logits=False)
+        # equal shards (2 rows over 2 ranks): the gather goes straight into the output tensor
+        logits2, _ = sharding.forward_sharded(fwd, torch.from_numpy(idx[:2]), torch.from_numpy(targets[:2]))
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=logits.numpy(), loss=loss.item(),
-                 loss1=loss1.item(), raised=raised)
+                 loss1=loss1.item(), raised=raised, logits2=logits2.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -93,6 +95,7 @@ def test_forward_sharded_world2_matches_unsharded(golden):
     cfg = O.OracleConfig(**SMALL)
     ref_logits, ref_loss, _ = O.efficient_ngpt_forward(cfg, weights, idx, targets)
     _, ref_loss1, _ = O.efficient_ngpt_forward(cfg, weights, idx[:1], targets[:1])
+    ref_logits2, _, _ = O.efficient_ngpt_forward(cfg, weights, idx[:2], targets[:2])
 
     ctx = mp.get_context("spawn")
     port = _free_port()
@@ -113,3 +116,4 @@ def test_forward_sharded_world2_matches_unsharded(golden):
         assert abs(float(r["loss"]) - ref_loss) <= 1e-6 * abs(ref_loss)  # combined in fp64, returned fp32
         assert abs(float(r["loss1"]) - ref_loss1) <= 1e-6 * abs(ref_loss1)
         assert bool(r["raised"])
+        np.testing.assert_allclose(r["logits2"], ref_logits2, rtol=1e-12, atol=1e-12)
