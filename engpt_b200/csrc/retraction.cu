@@ -173,7 +173,30 @@ __global__ void __launch_bounds__(kColWarps * 32) cols_apply_kernel(T* __restric
   const bool in0 = c0 < cols, in1 = c0 + 1 < cols;
   int64_t r0, r1;
   split_rows(rows, gridDim.y, blockIdx.y, r0, r1);
-  for (int64_t r = r0 + warp; r < r1; r += kColWarps) {
+  // four rows per iteration, every load issued before the first store, so each warp keeps several rows'
+  // reads in flight (one row at a time left the pass latency-bound); the same arithmetic per element
+  constexpr int U = 4;
+  int64_t r = r0 + warp;
+  for (; r + (U - 1) * kColWarps < r1; r += U * kColWarps) {
+    float v0[U], v1[U], g0[U], g1[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t o = (r + u * kColWarps) * cols + c0;
+      v0[u] = in0 ? ld1(x + o) : 0.f;
+      v1[u] = in1 ? ld1(x + o + 1) : 0.f;
+      if (PROJECT) {
+        g0[u] = in0 ? ld1(w + o) : 0.f;
+        g1[u] = in1 ? ld1(w + o + 1) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t o = (r + u * kColWarps) * cols + c0;
+      if (in0) st1(x + o, PROJECT ? fmaf(-k0, g0[u], v0[u]) : v0[u] / k0);
+      if (in1) st1(x + o + 1, PROJECT ? fmaf(-k1, g1[u], v1[u]) : v1[u] / k1);
+    }
+  }
+  for (; r < r1; r += kColWarps) {
     T* xr = x + r * cols;
     if (in0) {
       const float v = ld1(xr + c0);
